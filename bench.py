@@ -1,0 +1,277 @@
+"""Benchmark of the B200 token sampler on the headline configuration.
+
+Metric: sampled rows/sec and us per decode-step sample at
+B=256, V=248,320 (config 3: bf16 Zipf logits, top_p=0.95, T=1.0, Philox
+noise), and the fraction of the HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 3] [--mode philox|noise]
+
+A step is one sampler call over one batch of B rows resident in HBM.  L2 is
+not allowed to serve the logits: the timed loop rotates over enough distinct
+logits buffers to exceed twice the L2 size.  Multi-GPU (torchrun, NCCL):
+rows are sharded with no data-path collective (weak scaling: every rank
+samples its own B rows, keyed on its global row offset); time is the max
+over ranks.  ``--impl reference`` times the reference algorithm's CPU
+restatement (oracle/) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "sampled rows/sec at B=256, V=248,320 (config 3: Zipf bf16, top_p=0.95)"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([s.strip() for s in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def cpu_baseline(cfg: int, rows: int, seed_rows: int = 0):
+    """Time the oracle (CPU restatement of the reference sampler) on a bounded
+    sample of the workload with a spawn pool over all host cores."""
+    import multiprocessing as mp
+    from oracle import cpu_bench
+    cores = os.cpu_count() or 1
+    ctx = mp.get_context("spawn")
+    n = max(rows, cores)
+    with ctx.Pool(cores) as pool:
+        pool.map(cpu_bench.warm, range(cores))
+        t0 = time.perf_counter()
+        done = sum(pool.map(cpu_bench.sample_rows, [(cfg, i) for i in range(n)]))
+        dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "rows/s", "cores": cores, "kind": "port",
+            "sample": f"{done} rows of config {cfg} (V=248,320) through oracle/sampler_oracle.py, "
+                      f"one row per task on a {cores}-process spawn pool"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    per_step_rows = max(8, os.cpu_count() or 1)
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(args.config, per_step_rows)
+        if i >= args.warmup:
+            vals.append(r["value"])
+        base = r
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * 256 / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"config{args.config}", "B": 256, "V": 248320},
+            "cpu_baseline": dict(base, value=v),
+            "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=3)
+    ap.add_argument("--mode", default="philox", choices=["philox", "noise"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from qedge_b200 import workloads as W
+    from qedge_b200.sampler import QESampler
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    w = W.CONFIGS[args.config]()
+    B, V = w.B, w.V
+    row_offset = rank * B
+    esize = 4 if w.dtype == "f32" else 2
+    bytes_per_batch = B * V * esize
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / bytes_per_batch)) + 1)
+    base = W.to_device(w, dev)
+    bufs = [base] + [base.roll(shifts=i * 997, dims=1).contiguous() for i in range(1, nbuf)]
+    temps = torch.from_numpy(w.temperatures).to(dev)
+    tps = torch.from_numpy(w.top_ps).to(dev)
+    tks = torch.from_numpy(w.top_ks.astype(np.int32)).to(dev)
+    kw = {"top_ks": tks}
+    hist_bytes = 0
+    if w.history is not None:
+        kw.update(rep_penalties=torch.from_numpy(w.rep_penalties).to(dev),
+                  history=torch.from_numpy(w.history).to(dev),
+                  history_lens=torch.from_numpy(w.history_lens).to(dev))
+        hist_bytes = int(w.history_lens.sum()) * 4
+    noise = None
+    if args.mode == "noise":
+        noise = torch.from_numpy(W.exp_noise(B, V, 1)).to(dev)
+    sampler = QESampler(seed=1234)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        return sampler(bufs[i % nbuf], temps, tps, use_top_p=w.use_top_p, step=i,
+                       row_offset=row_offset, noise=noise, **kw)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    with clocks:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            per[i][0].record(stream)
+            step(args.warmup + i)
+            per[i][1].record(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    total_ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    ms = total_ms / args.steps
+    launch_ms = [a.elapsed_time(b) for a, b in per]
+
+    # end-to-end through the public API: pinned host logits -> device, sample,
+    # ids -> host, every step
+    host = torch.empty_like(base, device="cpu").pin_memory()
+    host.copy_(base)
+    out_host = torch.empty(B, dtype=torch.int64).pin_memory()
+    dbuf = torch.empty_like(base)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.e2e_steps):
+        dbuf.copy_(host, non_blocking=True)
+        ids = sampler(dbuf, temps, tps, use_top_p=w.use_top_p, step=10_000 + i,
+                      row_offset=row_offset, noise=noise, **kw)
+        out_host.copy_(ids, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    hbm, peak_kind = peaks()
+    alg_bytes = bytes_per_batch + hist_bytes + 8 * B + (B * V * 4 if noise is not None else 0)
+    med_launch = statistics.median(launch_ms)
+    achieved = alg_bytes / (med_launch * 1e-3) / 1e9
+    prof = ROOT / "profiles" / f"traffic_config{args.config}_{args.mode}.json"
+    traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch") if prof.exists() else None
+    if rank == 0:
+        line = {
+            "metric": METRIC if args.config == 3 else f"sampled rows/sec, config {args.config}",
+            "value": world * B / (ms * 1e-3), "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "us_per_sample_step": ms * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"bf16": "bf16", "f16": "f16", "f32": "f32"}[w.dtype] + " in, f32 math",
+            "data": "synthetic",
+            "config": {"workload": w.name, "B": B, "V": V, "noise": args.mode,
+                       "parallelism": f"rows x{world} (no collective)",
+                       "l2": f"rotating {nbuf} logits buffers ({nbuf * bytes_per_batch / 2**20:.0f} MiB > 2x L2)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "frac_of_8tbs": achieved / 8000.0, "traffic": traffic,
+                         "alg_bytes_per_launch": alg_bytes, "launch_us_median": med_launch * 1e3},
+            "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "rows/s",
+                    "h2d_bytes_per_step": bytes_per_batch, "d2h_bytes_per_step": 8 * B},
+            "gpu_launches": args.steps * 5,
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args.config, 16)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

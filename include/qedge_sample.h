@@ -1,0 +1,99 @@
+/*
+ * qedge_sample.h — C ABI of the B200 token sampler (libqesample.so).
+ *
+ * This library replaces the sampling step of QEdge's decode loop:
+ *   BatchSampler.forward(logits, temperatures, top_ps, *, all_greedy, use_top_p)
+ *   (reference: src/compute/sampler.py:25-41), called from
+ *   ModelRunner._sample_gpu (src/compute/model_runner.py:77-93) with the
+ *   per-row parameters packed by Batch._fill_sampling (src/data/batch.py:149-175).
+ *
+ * All pointers except `args` itself are device pointers unless stated.
+ * Functions never allocate device memory: scratch comes from the caller's
+ * workspace, sized by qe_sample_workspace_size().  They return a status
+ * code (QE_OK = 0, negative on error) and never abort; the message of the
+ * last error on the calling thread is returned by qe_last_error().
+ */
+#ifndef QEDGE_SAMPLE_H
+#define QEDGE_SAMPLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QE_ABI_VERSION 1
+
+/* element type of the logits rows */
+enum qe_dtype { QE_DTYPE_F32 = 0, QE_DTYPE_BF16 = 1, QE_DTYPE_F16 = 2 };
+
+/* qe_sample_args.flags */
+enum qe_flags {
+  QE_FLAG_ALL_GREEDY = 1u, /* BatchSampler.forward(all_greedy=True) (sampler.py:28-29) */
+  QE_FLAG_USE_TOP_P = 2u   /* BatchSampler.forward(use_top_p=True)  (sampler.py:34-38) */
+};
+
+/* status codes */
+enum qe_status {
+  QE_OK = 0,
+  QE_ERR_INVALID = -1,     /* bad argument (null pointer, size, alignment) */
+  QE_ERR_CUDA = -2,        /* a CUDA call or kernel launch failed */
+  QE_ERR_WORKSPACE = -3,   /* workspace missing or smaller than required */
+  QE_ERR_UNSUPPORTED = -4  /* a size this build does not handle */
+};
+
+/* per-row status bits written to out_status (when non-NULL) */
+enum qe_row_status {
+  QE_ROW_GREEDY = 1,       /* row sampled as greedy argmax (T <= 1e-5 or all_greedy) */
+  QE_ROW_NONFINITE = 2     /* probabilities not finite; greedy argmax returned */
+};
+
+typedef struct qe_sample_args {
+  uint32_t struct_size;        /* sizeof(qe_sample_args) (ABI check) */
+  int32_t dtype;               /* enum qe_dtype */
+  int64_t batch;               /* B rows */
+  int64_t vocab;               /* V ids per row, 1 <= V < 2^24 */
+  int64_t ld;                  /* row stride of logits in elements (>= V) */
+  const void* logits;          /* [B, ld] logits (sampler.py:25 `logits`) */
+  const float* temperatures;   /* [B] (sampler.py:25 `temperatures`; greedy iff <= 1e-5) */
+  const float* top_ps;         /* [B] or NULL (sampler.py:26 `top_ps`) */
+  const int32_t* top_ks;       /* [B] or NULL; <= 0 or >= V means off (batch.py:154-157) */
+  const float* rep_penalties;  /* [B] or NULL; repetition penalty over the history set */
+  const int32_t* history;      /* [B, history_ld] token ids or NULL */
+  const int32_t* history_lens; /* [B] valid entries per row, or NULL for all history_ld */
+  int64_t history_ld;
+  const float* noise;          /* [B, noise_ld] Exp(1) noise (parity mode) or NULL (Philox) */
+  int64_t noise_ld;
+  uint64_t seed;               /* Philox key */
+  uint64_t step;               /* Philox step (decode step) */
+  const uint64_t* step_ptr;    /* device step counter; overrides `step` when non-NULL */
+  int64_t row_offset;          /* global index of row 0 (keys the Philox stream) */
+  uint32_t flags;              /* enum qe_flags */
+  int64_t* out_ids;            /* [B] sampled token ids (int64, like torch.argmax) */
+  float* out_probs;            /* [B, probs_ld] softmax probabilities or NULL */
+  int64_t probs_ld;
+  int32_t* out_status;         /* [B] enum qe_row_status bits or NULL */
+  void* workspace;             /* device scratch, >= qe_sample_workspace_size() bytes */
+  size_t workspace_bytes;
+} qe_sample_args;
+
+/* ABI version of the loaded library (QE_ABI_VERSION). */
+int qe_abi_version(void);
+
+/* Bytes of device workspace qe_sample needs for a batch of B rows of V ids. */
+size_t qe_sample_workspace_size(int64_t batch, int64_t vocab);
+
+/* Sample one token per row on `stream` (a cudaStream_t; NULL = legacy default
+ * stream).  Replaces BatchSampler.forward (src/compute/sampler.py:25-41);
+ * asynchronous, no host synchronisation, no allocation. */
+int qe_sample(const qe_sample_args* args, void* stream);
+
+/* Message of the last error returned on this thread ("" if none). */
+const char* qe_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QEDGE_SAMPLE_H */

@@ -1,0 +1,96 @@
+"""ctypes binding of ``libqesample.so`` (the C ABI in ``include/qedge_sample.h``).
+
+The library is built in-tree by ``qedge_b200.build``.  There is no fallback:
+if the library cannot be loaded, every sampler call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqesample.so"
+
+QE_ABI_VERSION = 1
+QE_DTYPE_F32, QE_DTYPE_BF16, QE_DTYPE_F16 = 0, 1, 2
+QE_FLAG_ALL_GREEDY, QE_FLAG_USE_TOP_P = 1, 2
+QE_ROW_GREEDY, QE_ROW_NONFINITE = 1, 2
+STATUS_NAMES = {0: "QE_OK", -1: "QE_ERR_INVALID", -2: "QE_ERR_CUDA",
+                -3: "QE_ERR_WORKSPACE", -4: "QE_ERR_UNSUPPORTED"}
+
+# Every symbol the header declares; tests check the library exports them.
+EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error")
+
+_vp = ctypes.c_void_p
+
+
+class QeSampleArgs(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32),
+        ("batch", ctypes.c_int64),
+        ("vocab", ctypes.c_int64),
+        ("ld", ctypes.c_int64),
+        ("logits", _vp),
+        ("temperatures", _vp),
+        ("top_ps", _vp),
+        ("top_ks", _vp),
+        ("rep_penalties", _vp),
+        ("history", _vp),
+        ("history_lens", _vp),
+        ("history_ld", ctypes.c_int64),
+        ("noise", _vp),
+        ("noise_ld", ctypes.c_int64),
+        ("seed", ctypes.c_uint64),
+        ("step", ctypes.c_uint64),
+        ("step_ptr", _vp),
+        ("row_offset", ctypes.c_int64),
+        ("flags", ctypes.c_uint32),
+        ("out_ids", _vp),
+        ("out_probs", _vp),
+        ("probs_ld", ctypes.c_int64),
+        ("out_status", _vp),
+        ("workspace", _vp),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: Path | str | None = None) -> ctypes.CDLL:
+    """Load the sampler library (once) and declare its signatures."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise NativeError(f"{p} is missing: build it with `python -m qedge_b200.build`")
+        lib = ctypes.CDLL(str(p))
+        lib.qe_abi_version.restype = ctypes.c_int
+        lib.qe_abi_version.argtypes = []
+        lib.qe_sample_workspace_size.restype = ctypes.c_size_t
+        lib.qe_sample_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.qe_sample.restype = ctypes.c_int
+        lib.qe_sample.argtypes = [ctypes.POINTER(QeSampleArgs), _vp]
+        lib.qe_last_error.restype = ctypes.c_char_p
+        lib.qe_last_error.argtypes = []
+        ver = lib.qe_abi_version()
+        if ver != QE_ABI_VERSION:
+            raise NativeError(f"libqesample ABI {ver} != expected {QE_ABI_VERSION}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(rc: int, lib=None) -> None:
+    if rc != 0:
+        lib = lib or load()
+        msg = lib.qe_last_error().decode(errors="replace")
+        raise NativeError(f"{STATUS_NAMES.get(rc, rc)}: {msg}")

@@ -1,0 +1,100 @@
+// qe_abi.cu — the exported C ABI (include/qedge_sample.h): argument
+// validation, workspace layout and dispatch to the sampler kernels.
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "qe_internal.h"
+
+namespace qe {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t workspace_bytes(int64_t batch) {
+  size_t b = size_t(batch);
+  size_t n = 0;
+  n = align_up(n + b * kSlices * sizeof(SlicePart), 256);
+  n = align_up(n + b * sizeof(RowInfo), 256);
+  n = align_up(n + b * kSlices * sizeof(RacePart), 256);
+  return n;
+}
+
+Workspace carve_workspace(void* base, int64_t batch) {
+  char* p = static_cast<char*>(base);
+  size_t b = size_t(batch), n = 0;
+  Workspace w;
+  w.slices = reinterpret_cast<SlicePart*>(p + n);
+  n = align_up(n + b * kSlices * sizeof(SlicePart), 256);
+  w.rows = reinterpret_cast<RowInfo*>(p + n);
+  n = align_up(n + b * sizeof(RowInfo), 256);
+  w.race = reinterpret_cast<RacePart*>(p + n);
+  return w;
+}
+
+}  // namespace qe
+
+using namespace qe;
+
+extern "C" int qe_abi_version(void) { return QE_ABI_VERSION; }
+
+extern "C" const char* qe_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" size_t qe_sample_workspace_size(int64_t batch, int64_t vocab) {
+  (void)vocab;
+  return batch > 0 ? workspace_bytes(batch) : 0;
+}
+
+extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
+  g_last_error.clear();
+  if (!a) return set_error(QE_ERR_INVALID, "args is NULL");
+  if (a->struct_size != sizeof(qe_sample_args))
+    return set_error(QE_ERR_INVALID, "struct_size mismatch (header/library version skew)");
+  if (a->batch < 0) return set_error(QE_ERR_INVALID, "batch < 0");
+  if (a->batch == 0) return QE_OK;
+  if (a->vocab < 1 || a->vocab >= (int64_t(1) << 24))
+    return set_error(QE_ERR_INVALID, "vocab must be in [1, 2^24)");
+  if (a->ld < a->vocab) return set_error(QE_ERR_INVALID, "ld < vocab");
+  if (a->dtype != QE_DTYPE_F32 && a->dtype != QE_DTYPE_BF16 && a->dtype != QE_DTYPE_F16)
+    return set_error(QE_ERR_INVALID, "unknown dtype");
+  if (!a->logits || !a->temperatures || !a->out_ids)
+    return set_error(QE_ERR_INVALID, "logits, temperatures and out_ids are required");
+  if (a->noise && a->noise_ld < a->vocab) return set_error(QE_ERR_INVALID, "noise_ld < vocab");
+  if (a->out_probs && a->probs_ld < a->vocab) return set_error(QE_ERR_INVALID, "probs_ld < vocab");
+  if (a->history && a->history_ld < 0) return set_error(QE_ERR_INVALID, "history_ld < 0");
+  const bool pen = a->history && a->rep_penalties;
+  if (pen && a->vocab > 48 * 1024 * 32)
+    return set_error(QE_ERR_UNSUPPORTED, "repetition penalty supports vocab <= 1,572,864");
+  const size_t need = workspace_bytes(a->batch);
+  if (!a->workspace || a->workspace_bytes < need)
+    return set_error(QE_ERR_WORKSPACE, "workspace smaller than qe_sample_workspace_size()");
+  if (reinterpret_cast<uintptr_t>(a->workspace) % 256)
+    return set_error(QE_ERR_INVALID, "workspace must be 256-byte aligned");
+
+  KernelArgs ka;
+  ka.dtype = a->dtype;
+  ka.batch = a->batch; ka.vocab = a->vocab; ka.ld = a->ld;
+  ka.logits = a->logits;
+  ka.temperatures = a->temperatures;
+  ka.top_ps = a->top_ps;
+  ka.top_ks = a->top_ks;
+  ka.rep_penalties = a->rep_penalties;
+  ka.history = pen ? a->history : nullptr;
+  ka.history_lens = a->history_lens;
+  ka.history_ld = a->history_ld;
+  ka.noise = a->noise; ka.noise_ld = a->noise_ld;
+  ka.seed = a->seed; ka.step = a->step; ka.step_ptr = a->step_ptr;
+  ka.row_offset = a->row_offset;
+  ka.flags = a->flags;
+  ka.out_ids = a->out_ids;
+  ka.out_probs = a->out_probs; ka.probs_ld = a->probs_ld;
+  ka.out_status = a->out_status;
+  ka.ws = carve_workspace(a->workspace, a->batch);
+  return launch_ref_path(ka, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,80 @@
+// qe_internal.h — host/device structures shared by the sampler translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "qedge_sample.h"
+
+namespace qe {
+
+constexpr int kSlices = 8;
+
+// Per (row, slice) statistics written by the slice pass.
+struct alignas(32) SlicePart {
+  float ymax;               // max of logits/T over the slice
+  float xbest;              // greedy candidate value (penalised logits)
+  int64_t xbest_idx;        // its id (first index on ties, NaN maximal)
+  unsigned long long sfix;  // sum of fp32 group sums of exp(y - ymax), fixed point 2^-40
+  uint32_t flags;           // 1: NaN seen, 2: empty slice
+  uint32_t pad;
+};
+
+// Per-row state shared between passes.
+struct alignas(16) RowInfo {
+  float M, S;               // row max of logits/T and softmax normaliser
+  uint32_t status;          // enum qe_row_status
+  int32_t done;             // output already written (greedy / non-finite)
+  int32_t active;           // some top-k / top-p filter removes ids
+  int32_t k_on, p_on;
+  uint32_t pstar;           // fp32 bits of the smallest kept probability
+  long long tie_keep;       // kept ids among those with probability == pstar
+  long long tie_prefix[kSlices];  // ties with p == pstar in earlier slices
+};
+
+// Per (row, slice) race winner.
+struct alignas(16) RacePart {
+  float r;
+  int32_t pad;
+  int64_t id;
+};
+
+struct Workspace {
+  SlicePart* slices;
+  RowInfo* rows;
+  RacePart* race;
+};
+
+// Flattened, validated copy of qe_sample_args handed to the kernels.
+struct KernelArgs {
+  int32_t dtype;
+  int64_t batch, vocab, ld;
+  const void* logits;
+  const float* temperatures;
+  const float* top_ps;
+  const int32_t* top_ks;
+  const float* rep_penalties;
+  const int32_t* history;
+  const int32_t* history_lens;
+  int64_t history_ld;
+  const float* noise;
+  int64_t noise_ld;
+  uint64_t seed, step;
+  const uint64_t* step_ptr;
+  int64_t row_offset;
+  uint32_t flags;
+  int64_t* out_ids;
+  float* out_probs;
+  int64_t probs_ld;
+  int32_t* out_status;
+  Workspace ws;
+};
+
+size_t workspace_bytes(int64_t batch);
+Workspace carve_workspace(void* base, int64_t batch);
+
+int set_error(int code, const std::string& msg);
+int launch_ref_path(const KernelArgs& ka, cudaStream_t st);
+
+}  // namespace qe

@@ -128,3 +128,13 @@ def config5(B: int = 512, V: int = VOCAB, seed: int = 5) -> Workload:
 
 
 CONFIGS = {1: config1, 2: config2, 3: config3, 4: config4, 5: config5}
+
+
+def to_device(w: Workload, device="cuda"):
+    """Upload the logits of a workload as a torch tensor of its dtype."""
+    import torch
+    if w.dtype == "f32":
+        return torch.from_numpy(np.ascontiguousarray(w.logits_bits, np.float32)).to(device)
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16}[w.dtype]
+    t = torch.from_numpy(np.ascontiguousarray(w.logits_bits).view(np.int16)).to(device)
+    return t.view(dt)

@@ -1,0 +1,141 @@
+"""Token-id parity of the CUDA sampler with the reference and the oracle.
+
+* golden: ids produced by QEdge's own BatchSampler (tests/golden) must be
+  reproduced exactly by the kernel fed the same logits and noise;
+* oracle: extension features (top-k, repetition penalty) and Philox-mode
+  noise are checked against oracle/sampler_oracle.py bit-exactly;
+* probabilities: within 1e-5 relative of a float64 softmax.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import noise as ON
+from oracle import sampler_oracle as O
+from qedge_b200 import workloads as W
+from tests.golden import cases as C
+from tests.gpu_util import device_logits, run
+
+pytestmark = pytest.mark.gpu
+CASES = C.build_cases()
+
+
+@pytest.fixture(scope="module")
+def sampler():
+    from qedge_b200.sampler import QESampler
+    return QESampler(seed=0)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_golden_ids(name, sampler, golden):
+    w, spec = CASES[name]
+    g = golden["cases"][name]
+    if spec[0] == "exp":
+        ids = run(sampler, w, C.make_noise(spec, w.B, w.V), top_k=False)
+    else:
+        ids = run(sampler, w, None, seed=spec[1], step=spec[2], top_k=False)
+    np.testing.assert_array_equal(ids, np.asarray(g["ids"]))
+
+
+def oracle_ids(w, noise, top_k=True):
+    return O.sample(w.logits_f32(), w.temperatures, w.top_ps, noise,
+                    top_ks=w.top_ks if top_k else None, rep_penalties=w.rep_penalties,
+                    history=w.history, history_lens=w.history_lens,
+                    all_greedy=bool(np.all(w.temperatures <= 1e-5)), use_top_p=w.use_top_p)
+
+
+@pytest.mark.parametrize("cfg,B", [(2, 16), (4, 64), (5, 16)])
+@pytest.mark.parametrize("mode", ["exp", "philox"])
+def test_configs_vs_oracle(cfg, B, mode, sampler):
+    w = W.CONFIGS[cfg](B=B)
+    if mode == "exp":
+        noise = W.exp_noise(w.B, w.V, 100 + cfg)
+        ids = run(sampler, w, noise)
+    else:
+        noise = ON.philox_noise(w.B, w.V, seed=77 + cfg, step=3)
+        ids = run(sampler, w, None, seed=77 + cfg, step=3)
+    np.testing.assert_array_equal(ids, oracle_ids(w, noise))
+
+
+def test_full_config3_philox_vs_oracle_sample(sampler):
+    """Full headline batch (B=256) in Philox mode; the oracle checks 32 rows."""
+    w = W.config3()
+    ids = run(sampler, w, None, seed=2026, step=11)
+    rows = np.arange(0, 256, 8)
+    sub = W.Workload("sub", w.logits_bits[rows], "bf16", w.temperatures[rows], w.top_ps[rows],
+                     w.top_ks[rows], w.rep_penalties[rows], None, None, use_top_p=True)
+    noise = np.concatenate([ON.philox_noise(1, w.V, 2026, 11, row_offset=int(r)) for r in rows])
+    np.testing.assert_array_equal(ids[rows], oracle_ids(sub, noise))
+
+
+@pytest.mark.parametrize("V", [1, 2, 7, 8, 9, 255, 1023, 1025, 4096, 70001])
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+def test_small_vocab_edges(V, dtype, sampler):
+    g = np.random.Generator(np.random.PCG64(V))
+    B = 24
+    x = g.standard_normal((B, V), dtype=np.float32) * np.float32(2.0)
+    bits = {"bf16": W.to_bf16_bits(x), "f16": x.astype(np.float16).view(np.uint16), "f32": x}[dtype]
+    w = W.Workload("edge", bits, dtype, g.choice(np.array([0, 0.5, 1, 2], np.float32), size=B),
+                   g.uniform(0.05, 1.0, size=B).astype(np.float32),
+                   g.choice(np.array([0, 1, 2, 5, V], np.int32), size=B),
+                   np.full(B, 1.3, np.float32), g.integers(0, V, size=(B, 9)).astype(np.int32),
+                   g.integers(0, 10, size=B).astype(np.int32), use_top_p=True)
+    noise = W.exp_noise(B, V, 5)
+    np.testing.assert_array_equal(run(sampler, w, noise), oracle_ids(w, noise))
+    pn = ON.philox_noise(B, V, 3, 4)
+    np.testing.assert_array_equal(run(sampler, w, None, seed=3, step=4), oracle_ids(w, pn))
+
+
+def test_probabilities_match_f64_softmax(sampler):
+    w = W.config2(B=4)
+    probs = torch.empty(w.B, w.V, dtype=torch.float32, device="cuda")
+    run(sampler, w, W.exp_noise(w.B, w.V, 1), out_probs=probs)
+    got = probs.cpu().numpy().astype(np.float64)
+    x = C.penalised_f32(w)
+    for b in range(w.B):
+        want = O.probs_f64(x[b], float(w.temperatures[b]))
+        big = want > 1e-30
+        rel = np.abs(got[b][big] - want[big]) / want[big]
+        assert rel.max() < 1e-5, rel.max()
+
+
+def test_non_finite_rows_fall_back_to_greedy(sampler):
+    V = 1000
+    x = np.random.default_rng(0).standard_normal((4, V)).astype(np.float32)
+    x[0, 17] = np.nan
+    x[1, :] = -np.inf
+    x[2, 5] = np.inf
+    w = W.Workload("nf", x, "f32", np.ones(4, np.float32), np.full(4, 0.9, np.float32),
+                   np.zeros(4, np.int32), np.ones(4, np.float32), None, None, use_top_p=True)
+    st = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ids = run(sampler, w, W.exp_noise(4, V, 0), out_status=st)
+    assert ids[0] == 17 and ids[1] == 0 and ids[2] == 5
+    assert st.cpu().tolist()[:3] == [2, 2, 2] and st.cpu().tolist()[3] == 0
+
+
+def test_deterministic_and_keyed(sampler):
+    w = W.config3(B=16)
+    a = run(sampler, w, None, seed=5, step=1)
+    b = run(sampler, w, None, seed=5, step=1)
+    c = run(sampler, w, None, seed=5, step=2)
+    np.testing.assert_array_equal(a, b)
+    assert (a != c).any()
+
+
+def test_step_counter_on_device(sampler):
+    w = W.config3(B=8)
+    st = torch.tensor([9], dtype=torch.int64, device="cuda")
+    lg = device_logits(w)
+    ids = sampler(lg, torch.ones(8, device="cuda"), torch.full((8,), 0.95, device="cuda"),
+                  use_top_p=True, seed=1, step_tensor=st)
+    want = run(sampler, w, None, seed=1, step=9)
+    np.testing.assert_array_equal(ids.cpu().numpy(), want)
+
+
+def test_row_offset_keys_global_rows(sampler):
+    w = W.config3(B=8)
+    lg = device_logits(w)
+    t = torch.ones(8, device="cuda"); p = torch.full((8,), 0.95, device="cuda")
+    full = sampler(lg, t, p, use_top_p=True, seed=4, step=0)
+    half = sampler(lg[4:], t[4:], p[4:], use_top_p=True, seed=4, step=0, row_offset=4)
+    np.testing.assert_array_equal(full[4:].cpu().numpy(), half.cpu().numpy())
