@@ -58,8 +58,15 @@ def _rng(seed: int) -> np.random.Generator:
 
 def exp_noise(B: int, V: int, seed: int) -> np.ndarray:
     """Shared Exp(1) noise tensor for parity runs (the stand-in for the
-    generator behind ``torch.multinomial``)."""
-    return _rng(seed).standard_exponential((B, V), dtype=np.float32)
+    generator behind ``torch.multinomial``).
+
+    Exact zeros (float32 draws can round to 0) are raised to the smallest
+    normal float: the sampler contract is E > 0.  With E == 0 the reference's
+    race divides 0/0 for a token removed by top-p and ``torch.argmax`` picks
+    the NaN, i.e. it samples a token outside the nucleus.
+    """
+    e = _rng(seed).standard_exponential((B, V), dtype=np.float32)
+    return np.maximum(e, np.float32(np.finfo(np.float32).tiny))
 
 
 def config1(V: int = VOCAB, seed: int = 0) -> Workload:
