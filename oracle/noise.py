@@ -23,7 +23,9 @@ kernel skip generating noise for tokens that cannot win the race:
 * group ``G`` (32 tokens, layout below): ``E_min(G) = E_root`` if ``s`` is in
   ``G`` (and ``s`` is its argmin); otherwise
   ``E_min(G) = E_root + (-ln(u_G)) / n_G`` and a uniformly chosen member
-  carries it;
+  carries it.  The two groups of a tile pair (tiles 2q and 2q+1, same lane)
+  share one Philox call: words (x, y) for the even tile, (z, w) for the odd
+  one (first word -> u_G, second -> member selector);
 * every other token ``j`` of ``G``: ``E_j = E_min(G) + (-ln(u_j))``.
 
 By the memoryless property of the exponential distribution this is exactly
@@ -43,7 +45,7 @@ PHILOX_W0 = 0x9E3779B9
 PHILOX_W1 = 0xBB67AE85
 
 TAG_ROOT, TAG_GROUP, TAG_TOKEN = 0, 1, 2
-NSLICE = 8          # canonical vocab slices per row (also the max vocab-shard count)
+NSLICE = 16         # canonical vocab slices per row (also the max vocab-shard count)
 TILE = 1024         # ids per tile inside a slice
 GROUP_LANES = 32    # groups per tile
 
@@ -133,8 +135,8 @@ def slice_starts(V: int) -> np.ndarray:
 
 
 def group_layout(V: int):
-    """For every token id return (global group id, member index) and the
-    member count of every group.
+    """For every token id return (global group id, member index), the member
+    count of every group and every group's Philox (counter index, word pair).
 
     Inside slice g (ids [start, end)), the local offset o = j - start splits
     as tile t = o >> 10, block b = (o >> 8) & 3, lane l = (o >> 3) & 31,
@@ -145,7 +147,9 @@ def group_layout(V: int):
     gid = np.empty(V, dtype=np.int64)
     mem = np.empty(V, dtype=np.int64)
     sizes = []
+    ctrs = []
     base = 0
+    pair_base = 0
     for g in range(NSLICE):
         a, z = int(starts[g]), int(starts[g + 1])
         L = z - a
@@ -159,9 +163,13 @@ def group_layout(V: int):
         mem[a:z] = b * 8 + i
         cnt = np.bincount(t * GROUP_LANES + lane, minlength=ntiles * GROUP_LANES)
         sizes.append(cnt)
+        gt = np.arange(ntiles * GROUP_LANES, dtype=np.int64)
+        ctrs.append(np.stack([pair_base + (gt >> 6) * GROUP_LANES + (gt & 31), (gt >> 5) & 1], axis=1))
         base += ntiles * GROUP_LANES
+        pair_base += ((ntiles + 1) // 2) * GROUP_LANES
     sizes = np.concatenate(sizes) if sizes else np.zeros(0, np.int64)
-    return gid, mem, sizes.astype(np.int64)
+    ctrs = np.concatenate(ctrs) if ctrs else np.zeros((0, 2), np.int64)
+    return gid, mem, sizes.astype(np.int64), ctrs
 
 
 def _select(w1, w2, n):
@@ -173,6 +181,11 @@ def _select(w1, w2, n):
     return ((w1 * n + ((w2 * n) >> s32)) >> s32).astype(np.int64)
 
 
+def _select32(w, n):
+    """floor(w * n / 2^32) for n <= 2^24."""
+    return ((np.asarray(w, dtype=np.uint64) * np.asarray(n, dtype=np.uint64)) >> np.uint64(32)).astype(np.int64)
+
+
 def philox_noise(B: int, V: int, seed: int, step: int, row_offset: int = 0) -> np.ndarray:
     """Materialise the Exp(1) noise tensor E[B, V] that the kernel's Philox
     mode uses for rows row_offset .. row_offset+B-1."""
@@ -180,21 +193,23 @@ def philox_noise(B: int, V: int, seed: int, step: int, row_offset: int = 0) -> n
     k0, k1 = seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF
     s_lo = step & 0xFFFFFFFF
     hi = ((step >> 32) << 2) & 0xFFFFFFFF
-    gid, mem, sizes = group_layout(V)
+    gid, mem, sizes, ctrs = group_layout(V)
     NG = sizes.shape[0]
     Vf = np.float32(V)
     out = np.empty((B, V), dtype=np.float32)
-    garange = np.arange(NG, dtype=np.int64)
     jarange = np.arange(V, dtype=np.int64)
     for r in range(B):
         row = row_offset + r
         w = philox4x32_10(0, row, s_lo, hi | TAG_ROOT, k0, k1)
         e_root = (neglog_f32(uniform_open(w[0])) / Vf).astype(np.float32)
         s = int(_select(w[1], w[2], V))
-        wg = philox4x32_10(garange, row, s_lo, hi | TAG_GROUP, k0, k1)
+        wg = philox4x32_10(ctrs[:, 0], row, s_lo, hi | TAG_GROUP, k0, k1)
+        odd = ctrs[:, 1] == 1
+        w_u = np.where(odd, wg[2], wg[0])
+        w_s = np.where(odd, wg[3], wg[1])
         ng = np.maximum(sizes, 1).astype(np.float32)
-        e_min = (e_root + (neglog_f32(uniform_open(wg[0])) / ng).astype(np.float32)).astype(np.float32)
-        arg = _select(wg[1], wg[2], np.maximum(sizes, 1))
+        e_min = (e_root + (neglog_f32(uniform_open(w_u)) / ng).astype(np.float32)).astype(np.float32)
+        arg = _select32(w_s, np.maximum(sizes, 1))
         gs = gid[s]
         e_min[gs] = e_root
         arg[gs] = mem[s]

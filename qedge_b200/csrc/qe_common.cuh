@@ -15,7 +15,7 @@
 
 namespace qe {
 
-constexpr int kNumSlices = 8;          // canonical vocab slices per row (== kSlices)
+constexpr int kNumSlices = 16;         // canonical vocab slices per row (== kSlices)
 constexpr int kTile = 1024;            // ids per tile inside a slice
 constexpr int kGroupLanes = 32;        // groups per tile
 constexpr float kGreedyEps = 1e-5f;    // sampler.py:30 `temperatures <= 1e-5`
@@ -119,6 +119,10 @@ __device__ __forceinline__ uint32_t select_index(uint32_t hi, uint32_t lo, uint3
   uint64_t x = (uint64_t(hi) << 32) | lo;
   return uint32_t(__umul64hi(x, uint64_t(n)));
 }
+// floor(w * n / 2^32) for n <= 2^24.
+__device__ __forceinline__ uint32_t select_index32(uint32_t w, uint32_t n) {
+  return uint32_t((uint64_t(w) * n) >> 32);
+}
 // -ln(u) for u in [2^-24, 1); IEEE fp32 round-to-nearest, no contraction.
 // ln m = 2 atanh((m-1)/(m+1)) by its odd series after reduction to
 // m in [sqrt(1/2), sqrt(2)]; ln 2 split into a 15-bit head and a tail.
@@ -170,16 +174,23 @@ __device__ __forceinline__ NoiseRoot noise_root(const NoiseKey& k, int64_t V) {
   r.s = select_index(w.y, w.z, uint32_t(V));
   return r;
 }
-// Minimum of group `gid` (n members) and the member index that carries it.
+// Minimum of a group and the member index that carries it.  The two groups
+// of a tile pair share one Philox call (counter `ctr`): words (x, y) for the
+// even tile, (z, w) for the odd one.
 struct GroupMin { float e_min; int arg; };
+__device__ __forceinline__ GroupMin group_min_from(const NoiseRoot& root, uint32_t wu, uint32_t ws, int n) {
+  GroupMin g;
+  g.e_min = __fadd_rn(root.e_root, __fdiv_rn(neglog(uniform_open(wu)), float(n)));
+  g.arg = int(select_index32(ws, uint32_t(n)));
+  return g;
+}
 __device__ __forceinline__ GroupMin noise_group(const NoiseKey& k, const NoiseRoot& root,
-                                                int64_t gid, int n, int64_t gid_s, int mem_s) {
+                                                int64_t gid, uint32_t ctr, int odd, int n,
+                                                int64_t gid_s, int mem_s) {
   GroupMin g;
   if (gid == gid_s) { g.e_min = root.e_root; g.arg = mem_s; return g; }
-  U4 w = philox_at(k, uint32_t(gid), kTagGroup);
-  g.e_min = __fadd_rn(root.e_root, __fdiv_rn(neglog(uniform_open(w.x)), float(n)));
-  g.arg = int(select_index(w.y, w.z, uint32_t(n)));
-  return g;
+  U4 w = philox_at(k, ctr, kTagGroup);
+  return odd ? group_min_from(root, w.z, w.w, n) : group_min_from(root, w.x, w.y, n);
 }
 // Noise of token j (global id) that is member `mem` of a group with minimum g.
 __device__ __forceinline__ float noise_token(const NoiseKey& k, const GroupMin& g, int64_t j, int mem) {
@@ -210,5 +221,38 @@ __device__ __forceinline__ int64_t slice_group_base(int g, int64_t V) {
   for (int s = 0; s < g; ++s) base += slice_groups(slice_start(s + 1, V) - slice_start(s, V));
   return base;
 }
+// First Philox counter of slice g's group noise (one counter per tile pair
+// and lane).
+__host__ __device__ __forceinline__ int64_t slice_pair_base(int g, int64_t V) {
+  int64_t base = 0;
+  for (int s = 0; s < g; ++s) {
+    int64_t L = slice_start(s + 1, V) - slice_start(s, V);
+    base += (((L + kTile - 1) / kTile + 1) / 2) * kGroupLanes;
+  }
+  return base;
+}
+// Philox counter and word pair of local group lg of a slice.
+__host__ __device__ __forceinline__ uint32_t group_ctr(int64_t pair_base, int64_t lg) {
+  return uint32_t(pair_base + (lg >> 6) * kGroupLanes + (lg & 31));
+}
+__host__ __device__ __forceinline__ int group_odd(int64_t lg) { return int((lg >> 5) & 1); }
+
+// ---------------------------------------------------------------- softmax numerics
+// Canonical arithmetic of the sampler's softmax, shared by every kernel:
+//   c1 = RN(log2(e) / T);  for a slice with max xm: c0 = -RN(xm * c1)
+//   e_j = 2^fma(x_j, c1, c0)        (SFU ex2, within 2^-21 relative)
+//   fsum(G) = sequential fp32 sum of e_j over a group's members in order
+//   sfix(slice) = sum over groups of round(fsum(G) * 2^40)   (exact u64)
+//   S = sum over slices of sfix * 2^-40 * 2^(c0_slice - c0_row)   (double, slice order)
+//   p_j = RN(2^fma(x_j, c1, c0_row) / S)
+// which is softmax(x / T) up to ~1e-6 relative.
+__device__ __forceinline__ float qe_ex2(float a) {
+  float r;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ float temp_coef(float T) { return __fdiv_rn(1.4426950408889634f, T); }
+__device__ __forceinline__ float max_coef(float xm, float c1) { return -__fmul_rn(xm, c1); }
+__device__ __forceinline__ float unnorm(float x, float c1, float c0) { return qe_ex2(__fmaf_rn(x, c1, c0)); }
 
 }  // namespace qe

@@ -9,11 +9,11 @@
 
 namespace qe {
 
-constexpr int kSlices = 8;
+constexpr int kSlices = 16;
 
 // Per (row, slice) statistics written by the slice pass.
 struct alignas(32) SlicePart {
-  float ymax;               // max of logits/T over the slice
+  float ymax;               // max of the (penalised) logits over the slice
   float xbest;              // greedy candidate value (penalised logits)
   int64_t xbest_idx;        // its id (first index on ties, NaN maximal)
   unsigned long long sfix;  // sum of fp32 group sums of exp(y - ymax), fixed point 2^-40
@@ -23,7 +23,8 @@ struct alignas(32) SlicePart {
 
 // Per-row state shared between passes.
 struct alignas(16) RowInfo {
-  float M, S;               // row max of logits/T and softmax normaliser
+  float M, S;               // M: -RN(xmax * c1) (row exponent offset); S: softmax normaliser
+  float c1;                 // RN(log2(e) / T)
   uint32_t status;          // enum qe_row_status
   int32_t done;             // output already written (greedy / non-finite)
   int32_t active;           // some top-k / top-p filter removes ids

@@ -128,32 +128,28 @@ __global__ void __launch_bounds__(256) slice_stats_kernel(KernelArgs a) {
   __syncthreads();
 
   float xb = -INFINITY; int64_t ib = INT64_MAX;
-  float ymax = -INFINITY; bool nan = false;
+  float xmax = -INFINITY; bool nan = false;
   for (int64_t j = s0 + threadIdx.x; j < s1; j += blockDim.x) {
     float x = load_x<T>(a, row, j, smem_bits, s0, rp);
     if (argmax_better(x, j, xb, ib)) { xb = x; ib = j; }
-    if (!rp.greedy) {
-      float y = __fdiv_rn(x, rp.T);
-      nan |= (y != y);
-      ymax = fmaxf(ymax, y);
-    }
+    nan |= (x != x);
+    xmax = fmaxf(xmax, x);
   }
   block_argmax<256>(xb, ib, smf, smi);
   if (nan) snan = 1;
-  ymax = block_max<256>(ymax, smf);
+  xmax = block_max<256>(xmax, smf);
   SlicePart* part = a.ws.slices + row * kNumSlices + g;
   uint64_t total = 0;
-  const bool nonfinite = snan || !(ymax > -INFINITY) || ymax == INFINITY;
+  const float c1 = rp.greedy ? 0.f : temp_coef(rp.T);
+  const float c0 = max_coef(xmax, c1);
+  const bool nonfinite = snan || !(xmax > -INFINITY) || !(fabsf(c0) < INFINITY);
   if (!rp.greedy && !nonfinite) {
     const int64_t ng = slice_groups(L);
     for (int64_t lg = threadIdx.x; lg < ng; lg += blockDim.x) {
       float fs = 0.f;
       for (int m = 0; m < 32; ++m) {
         int64_t o = member_offset(lg, m);
-        if (o < L) {
-          float y = __fdiv_rn(load_x<T>(a, row, s0 + o, smem_bits, s0, rp), rp.T);
-          fs = __fadd_rn(fs, qe_exp(__fsub_rn(y, ymax)));
-        }
+        if (o < L) fs = __fadd_rn(fs, unnorm(load_x<T>(a, row, s0 + o, smem_bits, s0, rp), c1, c0));
       }
       if (fs > 0.f) atomicAdd(&ssum, (unsigned long long)__double2ull_rn(double(fs) * kSumScale));
     }
@@ -161,7 +157,7 @@ __global__ void __launch_bounds__(256) slice_stats_kernel(KernelArgs a) {
     total = ssum;
   }
   if (threadIdx.x == 0) {
-    part->ymax = ymax;
+    part->ymax = xmax;
     part->xbest = xb;
     part->xbest_idx = ib;
     part->sfix = total;
@@ -191,13 +187,17 @@ __global__ void row_reduce_kernel(KernelArgs a) {
   } else if (nan || !(M > -INFINITY) || M == INFINITY) {
     status = QE_ROW_NONFINITE;
   } else {
+    const float c1 = temp_coef(rp.T);
+    const float nM = max_coef(M, c1);
     double S = 0.0;
     for (int g = 0; g < kNumSlices; ++g) {
       if ((sp[g].flags & 2u) || !(sp[g].ymax > -INFINITY)) continue;
-      S += double(sp[g].sfix) * (1.0 / kSumScale) * exp(double(sp[g].ymax) - double(M));
+      S += double(sp[g].sfix) * (1.0 / kSumScale) * exp2(double(max_coef(sp[g].ymax, c1)) - double(nM));
     }
-    ri->M = M;
+    ri->M = nM;
+    ri->c1 = c1;
     ri->S = float(S);
+    if (!(fabsf(nM) < INFINITY)) status = QE_ROW_NONFINITE;
     const int64_t V = a.vocab;
     int k = a.top_ks ? a.top_ks[row] : 0;
     bool k_on = k > 0 && int64_t(k) < V;
@@ -206,6 +206,7 @@ __global__ void row_reduce_kernel(KernelArgs a) {
     ri->active = (k_on || p_on) ? 1 : 0;
     ri->k_on = k_on; ri->p_on = p_on;
     if (!(ri->S > 0.f) || ri->S == INFINITY) status = QE_ROW_NONFINITE;
+    if (status) ri->active = 0;
   }
   ri->status = status;
   if (status) {
@@ -220,9 +221,8 @@ __global__ void row_reduce_kernel(KernelArgs a) {
 // --------------------------------------------------------------- kernel 3
 template <typename T>
 __device__ __forceinline__ float prob_at(const KernelArgs& a, int64_t row, int64_t j, const uint32_t* bits,
-                                         const RowParams& rp, float M, float S) {
-  float y = __fdiv_rn(load_x<T>(a, row, j, bits, 0, rp), rp.T);
-  return __fdiv_rn(qe_exp(__fsub_rn(y, M)), S);
+                                         const RowParams& rp, float c1, float M, float S) {
+  return __fdiv_rn(unnorm(load_x<T>(a, row, j, bits, 0, rp), c1, M), S);
 }
 
 template <typename T>
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(1024) threshold_kernel(KernelArgs a) {
   const RowParams rp = row_params(a, row);
   const int64_t V = a.vocab;
   if (rp.pen) build_bitmap(smem_bits, (V + 31) / 32, rp.hist, rp.hlen, 0, V);
-  const float M = ri->M, S = ri->S;
+  const float M = ri->M, S = ri->S, c1 = ri->c1;
   const int k = a.top_ks ? a.top_ks[row] : 0;
   const int64_t n_k = ri->k_on ? int64_t(k) : V;
   int64_t n_keep = n_k;
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(1024) threshold_kernel(KernelArgs a) {
       __syncthreads();
       const uint32_t pre = s_prefix, msk = s_mask;
       for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
-        float p = prob_at<T>(a, row, j, smem_bits, rp, M, S);
+        float p = prob_at<T>(a, row, j, smem_bits, rp, c1, M, S);
         uint32_t key = __float_as_uint(p);
         if ((key & msk) == pre) {
           int b = (key >> shift) & 255;
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(1024) threshold_kernel(KernelArgs a) {
       __syncthreads();
       const uint32_t pre = s_prefix, msk = s_mask;
       for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
-        uint32_t key = __float_as_uint(prob_at<T>(a, row, j, smem_bits, rp, M, S));
+        uint32_t key = __float_as_uint(prob_at<T>(a, row, j, smem_bits, rp, c1, M, S));
         if ((key & msk) == pre) atomicAdd(&hc[(key >> shift) & 255], 1u);
       }
       __syncthreads();
@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(1024) threshold_kernel(KernelArgs a) {
     const int64_t s0 = slice_start(g, V), s1 = slice_start(g + 1, V);
     unsigned long long cnt = 0;
     for (int64_t j = s0 + threadIdx.x; j < s1; j += blockDim.x)
-      cnt += __float_as_uint(prob_at<T>(a, row, j, smem_bits, rp, M, S)) == pstar;
+      cnt += __float_as_uint(prob_at<T>(a, row, j, smem_bits, rp, c1, M, S)) == pstar;
     if (cnt) atomicAdd(&s_tie[g], cnt);
   }
   __syncthreads();
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
   const int64_t s0 = slice_start(g, V), s1 = slice_start(g + 1, V), L = s1 - s0;
   const RowParams rp = row_params(a, row);
   if (rp.pen) build_bitmap(smem_bits, (L + 31) / 32, rp.hist, rp.hlen, s0, s1);
-  const float M = ri->M, S = ri->S;
+  const float M = ri->M, S = ri->S, c1 = ri->c1;
   const bool active = ri->active;
   const uint32_t pstar = ri->pstar;
   const long long tie_keep = ri->tie_keep;
@@ -378,6 +378,7 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
     token_group(root.s, V, &gid_s, &mem_s);
   }
   const int64_t gbase = slice_group_base(g, V);
+  const int64_t pbase = slice_pair_base(g, V);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float rb = -INFINITY; int64_t ib = INT64_MAX;
   for (int64_t c0 = s0; c0 < s1; c0 += blockDim.x) {
@@ -385,8 +386,7 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
     const bool valid = j < s1;
     float p = 0.f;
     if (valid) {
-      float y = __fdiv_rn(load_x<T>(a, row, j, smem_bits, s0, rp), rp.T);
-      p = __fdiv_rn(qe_exp(__fsub_rn(y, M)), S);
+      p = __fdiv_rn(unnorm(load_x<T>(a, row, j, smem_bits, s0, rp), c1, M), S);
       if (a.out_probs) a.out_probs[row * a.probs_ld + j] = p;
     }
     bool in = valid;
@@ -411,7 +411,9 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
         const int64_t o = j - s0;
         const int64_t gid = gbase + local_group(o);
         const int mem = member_index(o);
-        const GroupMin gm = noise_group(key, root, gid, group_size(local_group(o), L), gid_s, mem_s);
+        const int64_t lg = local_group(o);
+        const GroupMin gm = noise_group(key, root, gid, group_ctr(pbase, lg), group_odd(lg),
+                                        group_size(lg, L), gid_s, mem_s);
         E = noise_token(key, gm, j, mem);
       }
       const float r = __fdiv_rn(p, E);

@@ -35,13 +35,16 @@ def test_neglog_accuracy():
 
 def test_group_layout_partitions_vocab():
     for V in (1, 7, 8, 1000, 1024, 4099, 248_320):
-        gid, mem, sizes = N.group_layout(V)
+        gid, mem, sizes, ctrs = N.group_layout(V)
         assert sizes.sum() == V
         assert np.all(np.bincount(gid, minlength=sizes.size) == sizes)
         # members are numbered 0..n-1 in increasing id order inside each group
         order = np.lexsort((np.arange(V), gid))
         ranks = np.arange(V) - np.searchsorted(gid[order], gid[order])
         assert np.all(mem[order] == ranks)
+        # every (Philox counter, word pair) is used by exactly one group
+        keys = ctrs[:, 0] * 2 + ctrs[:, 1]
+        assert np.unique(keys).size == keys.size
 
 
 def test_philox_noise_is_exp1():
