@@ -243,7 +243,7 @@ __host__ __device__ __forceinline__ int group_odd(int64_t lg) { return int((lg >
 //   e_j = 2^fma(x_j, c1, c0)        (SFU ex2, within 2^-21 relative)
 //   fsum(G) = sequential fp32 sum of e_j over a group's members in order
 //   sfix(slice) = sum over groups of round(fsum(G) * 2^40)   (exact u64)
-//   S = sum over slices of sfix * 2^-40 * 2^(c0_slice - c0_row)   (double, slice order)
+//   S = sum over slices of sfix * 2^-40 * 2^(c0_row - c0_slice)   (double, slice order)
 //   p_j = RN(2^fma(x_j, c1, c0_row) / S)
 // which is softmax(x / T) up to ~1e-6 relative.
 __device__ __forceinline__ float qe_ex2(float a) {

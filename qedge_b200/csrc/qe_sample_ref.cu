@@ -192,7 +192,7 @@ __global__ void row_reduce_kernel(KernelArgs a) {
     double S = 0.0;
     for (int g = 0; g < kNumSlices; ++g) {
       if ((sp[g].flags & 2u) || !(sp[g].ymax > -INFINITY)) continue;
-      S += double(sp[g].sfix) * (1.0 / kSumScale) * exp2(double(max_coef(sp[g].ymax, c1)) - double(nM));
+      S += double(sp[g].sfix) * (1.0 / kSumScale) * exp2(double(nM) - double(max_coef(sp[g].ymax, c1)));
     }
     ri->M = nM;
     ri->c1 = c1;
