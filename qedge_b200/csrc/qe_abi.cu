@@ -2,6 +2,8 @@
 // validation, workspace layout and dispatch to the sampler kernels.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "qe_internal.h"
@@ -23,6 +25,7 @@ size_t workspace_bytes(int64_t batch) {
   n = align_up(n + b * kSlices * sizeof(SlicePart), 256);
   n = align_up(n + b * sizeof(RowInfo), 256);
   n = align_up(n + b * kSlices * sizeof(RacePart), 256);
+  n = align_up(n + 256, 256);
   return n;
 }
 
@@ -35,6 +38,8 @@ Workspace carve_workspace(void* base, int64_t batch) {
   w.rows = reinterpret_cast<RowInfo*>(p + n);
   n = align_up(n + b * sizeof(RowInfo), 256);
   w.race = reinterpret_cast<RacePart*>(p + n);
+  n = align_up(n + b * kSlices * sizeof(RacePart), 256);
+  w.err = reinterpret_cast<int*>(p + n);
   return w;
 }
 
@@ -96,5 +101,14 @@ extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
   ka.out_probs = a->out_probs; ka.probs_ld = a->probs_ld;
   ka.out_status = a->out_status;
   ka.ws = carve_workspace(a->workspace, a->batch);
-  return launch_ref_path(ka, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // path choice: the fused cluster kernel unless QE_SAMPLER_PATH=ref, the
+  // debug probabilities are requested, or the vocabulary is too large
+  const char* env = std::getenv("QE_SAMPLER_PATH");
+  const int forced = (env && !std::strcmp(env, "ref")) ? 1 : (env && !std::strcmp(env, "fused")) ? 2 : 0;
+  const int cluster = a->dtype == QE_DTYPE_F32 ? 8 : 16;
+  const bool fused_ok = !a->out_probs && fused_capacity(a->vocab, cluster) > 0;
+  if (forced != 1 && fused_ok) return launch_fused(ka, st, cluster);
+  if (forced == 2 && !fused_ok && !a->out_probs) return set_error(QE_ERR_UNSUPPORTED, "QE_SAMPLER_PATH=fused but the fused path cannot take this call");
+  return launch_ref_path(ka, st);
 }

@@ -45,6 +45,7 @@ struct Workspace {
   SlicePart* slices;
   RowInfo* rows;
   RacePart* race;
+  int* err;                 // set non-zero by a kernel that hit a bounded-wait timeout
 };
 
 // Flattened, validated copy of qe_sample_args handed to the kernels.
@@ -77,5 +78,7 @@ Workspace carve_workspace(void* base, int64_t batch);
 
 int set_error(int code, const std::string& msg);
 int launch_ref_path(const KernelArgs& ka, cudaStream_t st);
+int fused_capacity(int64_t V, int cluster);
+int launch_fused(const KernelArgs& ka, cudaStream_t st, int cluster);
 
 }  // namespace qe

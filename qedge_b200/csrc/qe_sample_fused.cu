@@ -1,0 +1,1463 @@
+// qe_sample_fused.cu — the fused single-pass sampler (one thread-block
+// cluster per row, the row resident in the cluster's shared memory).
+//
+// Replaces BatchSampler.forward (src/compute/sampler.py:25-41) for rows
+// whose CTA share fits in shared memory.  Every row is read from HBM once,
+// by 1-D bulk copies (cp.async.bulk + mbarrier), into the shared memory of
+// the 8 (or 16) CTAs of a cluster; CTA q holds canonical vocab slices
+// [qU, qU+U).  Per row:
+//
+//   pass A   group maxima (32 ids per lane group), NaN flags, greedy argmax
+//   race     lazy exponential race: a group's best ratio is bounded by
+//            max(e)/min(E); only groups whose bound can still win are
+//            expanded, using the minimum-first Philox noise tree
+//   exchange candidates over DSMEM (cluster barrier)
+//   pass B   canonical softmax sums and, for the few race candidates, the
+//            exact probability mass and rank of the tokens ahead of them
+//   exchange decide: the first candidate (in race order) inside the
+//            top-k / top-p set wins
+//
+// Rows with a small top-k, and the rare rows whose candidates all fall
+// outside the nucleus, gather every token above a proven lower bound of the
+// kept set and finish exactly in CTA 0 (sort + prefix mass + race).  Rows
+// that defeat that too are finished by CTA 0 alone over DSMEM with the
+// radix-select method of the multi-kernel path.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "qe_common.cuh"
+#include "qe_fused_util.cuh"
+#include "qe_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace qe {
+namespace fz {
+
+constexpr int kMaxR = 8;          // race candidates tracked per row
+constexpr int kMaxItems = 2;      // tile pairs a warp owns per row
+constexpr int kGatherCap = 1024;  // gathered keys per CTA
+constexpr int kSmallK = 64;       // top-k rows up to this k take the gather path
+constexpr uint32_t kWaitLimit = 1u << 26;
+
+enum RowType : int { kDone = 0, kRaceTest = 1, kGather = 2, kSlow = 3 };
+
+struct Cand {
+  float r;   // ratio e/E in the producing CTA's scale
+  float x;   // penalised logit
+  float E;   // noise
+  int id;    // token id
+};
+
+struct alignas(16) Share {
+  float umax[2];
+  float cmax;
+  float c0;
+  int nan;
+  int ncand;
+  int gidx;
+  float gval;
+  uint32_t topk_lkey;
+  int ngather;
+  int overflow;
+  int pad;
+  Cand cand[kMaxR];
+  unsigned long long sfix[2];
+  double F[kMaxR];
+  long long cnt[kMaxR];
+};
+
+struct RowState {
+  int type;
+  int out;
+  int status;
+  int R;
+  int p_on, k_on, k;
+  float tp;
+  float c1, nM, xM, Sf;
+  double S;
+  float L;               // gather lower bound (x' >= L)
+  float umax[16];        // every slice's max (for S)
+  Cand cand[kMaxR];      // global candidates, race order (approximate)
+  float rM[kMaxR];       // their exact ratios once S is known
+};
+
+template <int CL>
+struct Cfg {
+  static constexpr int NT = CL == 8 ? 512 : 256;
+  static constexpr int NW = NT / 32;
+  static constexpr int U = 16 / CL;
+};
+
+struct FusedParams {
+  KernelArgs a;
+  int nclusters;
+  int cap;         // data capacity in elements (multiple of 256)
+  int tma_ok;      // logits rows 16-byte aligned
+  int noise_vec;   // noise rows 16-byte aligned
+  int merge_cap;   // keys CTA 0 can sort in its data buffer (power of two)
+};
+
+// ---------------------------------------------------------------- smem layout
+template <typename T, int CL>
+struct Smem {
+  static constexpr int NW = Cfg<CL>::NW;
+  static __host__ __device__ size_t data_bytes(int cap) { return size_t(cap) * sizeof(T); }
+  static __host__ __device__ size_t pen_off(int cap) { return (data_bytes(cap) + 127) / 128 * 128; }
+  static __host__ __device__ size_t gather_off(int cap) { return pen_off(cap) + ((cap / 32 + 1) * 4 + 15) / 16 * 16; }
+  static __host__ __device__ size_t share_off(int cap) { return gather_off(cap) + kGatherCap * 8; }
+  static __host__ __device__ size_t wl_off(int cap) { return share_off(cap) + 2 * sizeof(Share); }
+  static __host__ __device__ size_t rs_off(int cap) { return wl_off(cap) + size_t(NW) * kMaxR * sizeof(Cand); }
+  static __host__ __device__ size_t misc_off(int cap) { return (rs_off(cap) + sizeof(RowState) + 15) / 16 * 16; }
+  static __host__ __device__ size_t total(int cap);
+};
+
+struct Misc {
+  uint64_t mbar;
+  unsigned int umaxkey[2];
+  int nan;
+  unsigned int gmin;
+  int err;
+  int ngather;
+  int overflow;
+  float theta;
+  unsigned int wtop[16 * 8];
+  float wF[16][kMaxR];
+  long long wcnt[16][kMaxR];
+  unsigned long long wsfix[16][2];
+  int slow_int[48];
+};
+
+template <typename T, int CL>
+__host__ __device__ size_t Smem<T, CL>::total(int cap) {
+  return misc_off(cap) + (sizeof(Misc) + 127) / 128 * 128;
+}
+
+// ---------------------------------------------------------------- small helpers
+__device__ __forceinline__ int ctz_lane(uint32_t m) { return __ffs(m) - 1; }
+
+// Insert (c) into a list sorted by race order, keeping the best n.
+__device__ __forceinline__ void list_insert(Cand* l, int n, const Cand& c) {
+  if (!rbetter(c.r, c.id, l[n - 1].r, l[n - 1].id)) return;
+  int i = n - 1;
+  while (i > 0 && rbetter(c.r, c.id, l[i - 1].r, l[i - 1].id)) { l[i] = l[i - 1]; --i; }
+  l[i] = c;
+}
+
+// Warp-level: merge the 32 lanes' (r, x, E, id) into the warp list (lane 0
+// owns the list in shared memory).  At most n rounds.
+__device__ __forceinline__ void warp_merge(Cand* wl, int n, float r, float x, float E, int id) {
+  const int lane = threadIdx.x & 31;
+  for (int round = 0; round < n; ++round) {
+    float br = r; int bid = id; int bl = lane;
+    for (int o = 16; o; o >>= 1) {
+      float orr = __shfl_xor_sync(0xffffffffu, br, o);
+      int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+      int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      if (rbetter(orr, oid, br, bid) || (!rbetter(br, bid, orr, oid) && ol < bl)) { br = orr; bid = oid; bl = ol; }
+    }
+    if (!(br > -INFINITY)) break;
+    const float bx = __shfl_sync(0xffffffffu, x, bl);
+    const float bE = __shfl_sync(0xffffffffu, E, bl);
+    bool full_and_worse = false;
+    if (lane == 0) {
+      full_and_worse = !rbetter(br, bid, wl[n - 1].r, wl[n - 1].id);
+      if (!full_and_worse) list_insert(wl, n, Cand{br, bx, bE, bid});
+    }
+    full_and_worse = __shfl_sync(0xffffffffu, full_and_worse, 0);
+    __syncwarp();
+    if (full_and_worse) break;
+    if (lane == bl) r = -INFINITY;
+  }
+}
+
+// ---------------------------------------------------------------- per-row geometry
+struct Geo {
+  int64_t cta_start, cta_end;  // global ids held by this CTA
+  int64_t ustart[2], uend[2];  // global ids of each unit (slice)
+  int uoff[2];                 // CTA-local element offset of each unit
+  int L[2];
+  int ntiles[2], npairs[2];
+  int nitems;
+  int64_t gbase[2], pbase[2];  // group id / Philox counter bases of each unit
+};
+
+template <int U>
+__device__ __forceinline__ Geo make_geo(int q, int64_t V) {
+  Geo g;
+  g.cta_start = slice_start(q * U, V);
+  g.cta_end = slice_start(q * U + U, V);
+  g.nitems = 0;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    if (u < U) {
+      const int s = q * U + u;
+      g.ustart[u] = slice_start(s, V);
+      g.uend[u] = slice_start(s + 1, V);
+      g.uoff[u] = int(g.ustart[u] - g.cta_start);
+      g.L[u] = int(g.uend[u] - g.ustart[u]);
+      g.ntiles[u] = (g.L[u] + kTile - 1) / kTile;
+      g.npairs[u] = (g.ntiles[u] + 1) / 2;
+      g.gbase[u] = slice_group_base(s, V);
+      g.pbase[u] = slice_pair_base(s, V);
+      g.nitems += g.npairs[u];
+    } else {
+      g.ustart[u] = g.uend[u] = g.cta_end;
+      g.uoff[u] = 0; g.L[u] = 0; g.ntiles[u] = 0; g.npairs[u] = 0; g.gbase[u] = 0; g.pbase[u] = 0;
+    }
+  }
+  return g;
+}
+__device__ __forceinline__ void item_of(const Geo& g, int item, int& u, int& p) {
+  if (item < g.npairs[0]) { u = 0; p = item; } else { u = 1; p = item - g.npairs[0]; }
+}
+struct Unit {
+  int L, uoff, ntiles;
+  int64_t ustart, uend, gbase, pbase;
+};
+__device__ __forceinline__ Unit unit_of(const Geo& g, int u) {
+  Unit r;
+  r.L = u ? g.L[1] : g.L[0];
+  r.uoff = u ? g.uoff[1] : g.uoff[0];
+  r.ntiles = u ? g.ntiles[1] : g.ntiles[0];
+  r.ustart = u ? g.ustart[1] : g.ustart[0];
+  r.uend = u ? g.uend[1] : g.uend[0];
+  r.gbase = u ? g.gbase[1] : g.gbase[0];
+  r.pbase = u ? g.pbase[1] : g.pbase[0];
+  return r;
+}
+// Warp-aggregated append of the flagged elements (bit i of `mask` flags
+// element off+i) as (ordered key, inverted id) pairs.  All 32 lanes call it.
+__device__ __forceinline__ void gather_append(unsigned mask, const float x[8], int64_t id0,
+                                              unsigned long long* gath, int* counter) {
+  const int lane = threadIdx.x & 31;
+  const int cnt = __popc(mask);
+  int incl = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (!total) return;
+  int base = 0;
+  if (lane == 31) base = atomicAdd(counter, total);
+  base = __shfl_sync(0xffffffffu, base, 31);
+  int pos = base + incl - cnt;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if ((mask >> i) & 1u) {
+      if (pos < kGatherCap) {
+        const uint32_t id = uint32_t(id0 + i);
+        gath[pos] = (uint64_t(ordered_key(x[i])) << 32) | uint64_t(0xFFFFFFFFu - id);
+      }
+      ++pos;
+    }
+}
+
+// Penalised logit of CTA-local element `off` (scalar path).
+template <typename T>
+__device__ __forceinline__ float load1(const void* buf, const uint32_t* pen, bool use_pen, float rp, int off) {
+  float x;
+  if constexpr (sizeof(T) == 4) {
+    x = static_cast<const float*>(buf)[off];
+  } else if constexpr (std::is_same<T, __half>::value) {
+    x = __half2float(static_cast<const __half*>(buf)[off]);
+  } else {
+    x = __uint_as_float(uint32_t(static_cast<const uint16_t*>(buf)[off]) << 16);
+  }
+  if (use_pen && ((pen[off >> 5] >> (off & 31)) & 1u)) x = penalise(x, rp);
+  return x;
+}
+
+// Noise of global token j under the Philox tree (any CTA can evaluate it).
+__device__ __forceinline__ float tree_noise(const NoiseKey& key, const NoiseRoot& root, int64_t gid_s,
+                                            int mem_s, int64_t j, int64_t V) {
+  int s = 0;
+  while (s + 1 < kNumSlices && slice_start(s + 1, V) <= j) ++s;
+  const int64_t a = slice_start(s, V), L = slice_start(s + 1, V) - a;
+  const int64_t o = j - a, lg = local_group(o);
+  const GroupMin gm = noise_group(key, root, slice_group_base(s, V) + lg, group_ctr(slice_pair_base(s, V), lg),
+                                  group_odd(lg), group_size(lg, L), gid_s, mem_s);
+  return noise_token(key, gm, j, member_index(o));
+}
+
+// Bitonic sort (descending) of n = power of two 64-bit keys in shared memory.
+template <int NT>
+__device__ void bitonic_desc(unsigned long long* k, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n / 2; i += NT) {
+        const int lo = 2 * stride * (i / stride) + (i % stride);
+        const int hi = lo + stride;
+        const bool desc = ((lo & size) == 0);
+        const unsigned long long a = k[lo], b = k[hi];
+        if ((a < b) == desc) { k[lo] = b; k[hi] = a; }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+template <typename T, int CL>
+struct Kernel {
+  static constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
+  using S = Smem<T, CL>;
+};
+
+// Exact finish of one row by CTA 0 alone, reading every CTA's slice over
+// DSMEM (the peers wait at a cluster barrier meanwhile).  The kept set is
+// found by radix selection on the ordered logit keys, with integer counts
+// (top-k) and probability masses in 2^-62 fixed point (top-p), as in the
+// multi-kernel path; then the race runs over the kept ids in id order.
+template <typename T, int CL>
+__device__ void slow_exact(const FusedParams& P, int64_t row, cg::cluster_group& cluster, void* data,
+                           uint32_t* pen, unsigned long long* scratch, const RowState& rs, bool use_pen,
+                           float rpv, int* s_int) {
+  constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
+  const KernelArgs& a = P.a;
+  const int64_t V = a.vocab;
+  const float c1 = rs.c1, nM = rs.nM, Sf = rs.Sf;
+  uint32_t* hc = reinterpret_cast<uint32_t*>(scratch);
+  unsigned long long* hm = scratch + 128;  // 256 u64 after 256 u32
+  int& s_bin = s_int[0];
+  long long* s_ll = reinterpret_cast<long long*>(s_int + 2);  // [0] cbase [1] mbase
+  uint32_t* s_u = reinterpret_cast<uint32_t*>(s_int + 8);     // [0] prefix [1] mask
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  auto for_all = [&](auto&& f) {
+    for (int r = 0; r < CL; ++r) {
+      const int64_t s0 = slice_start(r * U, V), s1 = slice_start(r * U + U, V);
+      const void* d = cluster.map_shared_rank(data, r);
+      const uint32_t* pb = cluster.map_shared_rank(pen, r);
+      for (int off = threadIdx.x; off < int(s1 - s0); off += NT) f(s0 + off, load1<T>(d, pb, use_pen, rpv, off));
+    }
+  };
+  auto prob = [&](float x) { return __fdiv_rn(unnorm(x, c1, nM), Sf); };
+
+  // radix select: weighted (top-p) or counting (top-k)
+  auto select = [&](bool weighted, unsigned long long Tfix, long long pos, uint32_t& key_out, long long& keep_out) {
+    if (threadIdx.x == 0) { s_u[0] = 0; s_u[1] = 0; s_ll[0] = 0; s_ll[1] = 0; }
+    __syncthreads();
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = threadIdx.x; b < 256; b += NT) { hc[b] = 0; hm[b] = 0; }
+      __syncthreads();
+      const uint32_t pre = s_u[0], msk = s_u[1];
+      for_all([&](int64_t, float x) {
+        const uint32_t kq = ordered_key(x);
+        if ((kq & msk) == pre) {
+          const int b = (kq >> shift) & 255;
+          atomicAdd(&hc[b], 1u);
+          if (weighted) atomicAdd(&hm[b], (unsigned long long)__double2ull_rn(double(prob(x)) * kMassScale));
+        }
+      });
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        long long c = s_ll[0];
+        unsigned long long m = (unsigned long long)s_ll[1];
+        int cand = -1;
+        long long cc = c;
+        unsigned long long cm = m;
+        for (int b = 255; b >= 0; --b) {
+          if (hc[b] == 0) continue;
+          if (weighted) {
+            if (m <= Tfix) { cand = b; cc = c; cm = m; } else break;
+          } else {
+            if (pos < c + (long long)hc[b]) { cand = b; cc = c; break; }
+          }
+          m += hm[b];
+          c += hc[b];
+        }
+        if (cand < 0) cand = 0;
+        s_bin = cand;
+        s_u[0] = pre | (uint32_t(cand) << shift);
+        s_u[1] = msk | (255u << shift);
+        s_ll[0] = cc;
+        s_ll[1] = (long long)cm;
+      }
+      __syncthreads();
+    }
+    key_out = s_u[0];
+    const long long nt = hc[s_bin & 255];
+    if (weighted) {
+      const unsigned long long f = __double2ull_rn(double(prob(key_to_float(key_out))) * kMassScale);
+      long long c = nt;
+      if (f > 0) {
+        const unsigned long long room = Tfix - (unsigned long long)s_ll[1];
+        const unsigned long long qq = room / f + 1;
+        if (qq < (unsigned long long)nt) c = (long long)qq;
+      }
+      keep_out = s_ll[0] + c;  // number of kept tokens
+    } else {
+      keep_out = pos + 1;
+    }
+    __syncthreads();
+  };
+
+  long long n_keep = V;
+  uint32_t vkey = 0;
+  bool have = false;
+  if (rs.p_on) {
+    const unsigned long long Tfix = (unsigned long long)(double(rs.tp) * kMassScale);
+    select(true, Tfix, 0, vkey, n_keep);
+    have = true;
+  }
+  if (rs.k_on && rs.k < n_keep) {
+    select(false, 0ull, rs.k - 1, vkey, n_keep);
+    have = true;
+  }
+  // tokens strictly above vkey are kept; ties at vkey are kept in id order
+  // until n_keep tokens are kept
+  long long above = 0;
+  if (have) {
+    if (threadIdx.x == 0) s_ll[0] = 0;
+    __syncthreads();
+    long long cnt = 0;
+    for_all([&](int64_t, float x) { cnt += ordered_key(x) > vkey; });
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&s_ll[0]), (unsigned long long)cnt);
+    __syncthreads();
+    above = s_ll[0];
+    __syncthreads();
+  }
+  const long long tie_keep = have ? n_keep - above : 0;
+  // race over the kept ids in id order (tie rank by a running block scan)
+  const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+  const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
+  NoiseRoot rt{0.f, 0};
+  int64_t gs = -1;
+  int mem_s = 0;
+  if (!a.noise) {
+    rt = noise_root(key, V);
+    token_group(rt.s, V, &gs, &mem_s);
+  }
+  int* wt = s_int + 16;  // per-warp tie counts
+  long long tie_base = 0;
+  float br = -INFINITY;
+  int bid = 0x7FFFFFFF;
+  for (int r = 0; r < CL; ++r) {
+    const int64_t s0 = slice_start(r * U, V), s1 = slice_start(r * U + U, V);
+    const void* d = cluster.map_shared_rank(data, r);
+    const uint32_t* pb = cluster.map_shared_rank(pen, r);
+    for (int base = 0; base < int(s1 - s0); base += NT) {
+      const int off = base + threadIdx.x;
+      const bool valid = off < int(s1 - s0);
+      const float x = valid ? load1<T>(d, pb, use_pen, rpv, off) : -INFINITY;
+      const uint32_t kq = ordered_key(x);
+      const bool tie = have && valid && kq == vkey;
+      const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+      if (lane == 0) wt[warp] = __popc(bal);
+      __syncthreads();
+      int before = 0, total = 0;
+      for (int w = 0; w < NW; ++w) { if (w < warp) before += wt[w]; total += wt[w]; }
+      const long long trank = tie_base + before + __popc(bal & ((1u << lane) - 1u));
+      const bool in = valid && (!have || kq > vkey || (tie && trank < tie_keep));
+      if (in) {
+        const int64_t j = s0 + off;
+        const float pv = prob(x);
+        const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + j) : tree_noise(key, rt, gs, mem_s, j, V);
+        const float rv = __fdiv_rn(pv, E);
+        if (rbetter(rv, int(j), br, bid)) { br = rv; bid = int(j); }
+      }
+      tie_base += total;
+      __syncthreads();
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float orr = __shfl_xor_sync(0xffffffffu, br, o);
+    const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+    if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; }
+  }
+  float* wr = reinterpret_cast<float*>(hm);
+  int* wi = reinterpret_cast<int*>(hm) + NW;
+  if (lane == 0) { wr[warp] = br; wi[warp] = bid; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
+    a.out_ids[row] = bid == 0x7FFFFFFF ? rs.out : bid;
+    if (a.out_status) a.out_status[row] = 0;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- the kernel
+template <typename T, int CL>
+__global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(FusedParams P) {
+  constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
+  using SM = Smem<T, CL>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const KernelArgs& a = P.a;
+  void* data = smem;
+  uint32_t* pen = reinterpret_cast<uint32_t*>(smem + SM::pen_off(P.cap));
+  unsigned long long* gath = reinterpret_cast<unsigned long long*>(smem + SM::gather_off(P.cap));
+  Share* share = reinterpret_cast<Share*>(smem + SM::share_off(P.cap));
+  Cand* wl_all = reinterpret_cast<Cand*>(smem + SM::wl_off(P.cap));
+  RowState& rs = *reinterpret_cast<RowState*>(smem + SM::rs_off(P.cap));
+  Misc& ms = *reinterpret_cast<Misc*>(smem + SM::misc_off(P.cap));
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = int(cluster.block_rank());
+  const int cid = int(blockIdx.x) / CL;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Cand* wl = wl_all + warp * kMaxR;
+  const int64_t V = a.vocab;
+  const Geo geo = make_geo<U>(q, V);
+  const int n_cta = int(geo.cta_end - geo.cta_start);
+  int ex = 0;  // exchange counter (alternating share slots)
+
+  if (threadIdx.x == 0) {
+    mbar_init(&ms.mbar, 1);
+    ms.err = 0;
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+
+  for (int64_t row = cid; row < a.batch; row += P.nclusters) {
+    // ------------------------------------------------------------ row parameters
+    const float T_ = a.temperatures[row];
+    const bool greedy = (a.flags & QE_FLAG_ALL_GREEDY) || !(T_ > kGreedyEps);
+    const int kk = a.top_ks ? a.top_ks[row] : 0;
+    const bool k_on = kk > 0 && int64_t(kk) < V;
+    const float tp = a.top_ps ? a.top_ps[row] : 1.f;
+    const bool p_on = (a.flags & QE_FLAG_USE_TOP_P) && a.top_ps && tp < 1.f;
+    const float rpv = a.rep_penalties ? a.rep_penalties[row] : 1.f;
+    int64_t hlen = 0;
+    const int32_t* hist = nullptr;
+    if (a.history) {
+      hist = a.history + row * a.history_ld;
+      hlen = a.history_lens ? a.history_lens[row] : a.history_ld;
+      if (hlen > a.history_ld) hlen = a.history_ld;
+      if (hlen < 0) hlen = 0;
+    }
+    const bool use_pen = hist && hlen > 0 && rpv != 1.f;
+    const bool small_k = !greedy && k_on && kk <= kSmallK && kk > 1;
+    const bool need_race = !greedy && !(k_on && kk == 1) && !small_k;
+    const float c1 = greedy ? 0.f : temp_coef(T_);
+
+    // ------------------------------------------------------------ load the CTA's share of the row
+    const unsigned char* src_row = static_cast<const unsigned char*>(a.logits) + row * a.ld * int64_t(sizeof(T));
+    const size_t nbytes = size_t(n_cta) * sizeof(T);
+    const size_t bulk = P.tma_ok ? (nbytes & ~size_t(15)) : 0;
+    if (threadIdx.x == 0) {
+      ms.nan = 0; ms.gmin = 0xFFFFFFFFu; ms.umaxkey[0] = ms.umaxkey[1] = 0u;
+      ms.ngather = 0; ms.overflow = 0;
+      if (bulk) {
+        fence_proxy_async();
+        mbar_expect_tx(&ms.mbar, uint32_t(bulk));
+        const unsigned char* src = src_row + geo.cta_start * int64_t(sizeof(T));
+        for (size_t o = 0; o < bulk; o += 32768) {
+          const uint32_t n = uint32_t((bulk - o) < 32768 ? (bulk - o) : 32768);
+          bulk_g2s(static_cast<unsigned char*>(data) + o, src + o, n, &ms.mbar);
+        }
+      }
+    }
+    // non-bulk part (unaligned rows or the ragged tail)
+    {
+      const T* src = reinterpret_cast<const T*>(src_row) + geo.cta_start;
+      T* dst = static_cast<T*>(data);
+      for (int i = int(bulk / sizeof(T)) + threadIdx.x; i < n_cta; i += NT) dst[i] = src[i];
+      // pad to a multiple of 8 elements (read as -inf by the 8-wide loads)
+    }
+    if (use_pen) {
+      const int nw = n_cta / 32 + 1;
+      for (int i = threadIdx.x; i < nw; i += NT) pen[i] = 0u;
+    }
+    __syncthreads();
+    if (use_pen) {
+      for (int64_t h = threadIdx.x; h < hlen; h += NT) {
+        const int64_t id = hist[h];
+        if (id >= geo.cta_start && id < geo.cta_end) {
+          const int off = int(id - geo.cta_start);
+          atomicOr(&pen[off >> 5], 1u << (off & 31));
+        }
+      }
+    }
+    if (bulk) {
+      if (!mbar_wait(&ms.mbar, phase, kWaitLimit)) ms.err = 1;
+      phase ^= 1u;
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------ pass A: group maxima
+    float gmax[kMaxItems][2];
+    float gEmin[kMaxItems][2];
+    bool lnan = false;
+#pragma unroll
+    for (int k = 0; k < kMaxItems; ++k) {
+      gmax[k][0] = gmax[k][1] = -INFINITY;
+      gEmin[k][0] = gEmin[k][1] = INFINITY;
+      const int item = warp + k * NW;
+      if (item < geo.nitems) {
+        int u, p;
+        item_of(geo, item, u, p);
+        const Unit un = unit_of(geo, u);
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * p + tt;
+          if (t < un.ntiles) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int local = t * kTile + b * 256 + lane * 8;
+              const int nv = un.L - local;
+              if (nv > 0) {
+                const int off = un.uoff + local;
+                float x[8];
+                Load8<T>::run(data, off, nv, x);
+                if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+                float m = gmax[k][tt];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) { m = fmaxf(m, x[i]); lnan |= (x[i] != x[i]); }
+                gmax[k][tt] = m;
+                if (a.noise && !greedy) {
+                  const float* nz = a.noise + row * a.noise_ld + geo.cta_start + off;
+                  float E[8];
+                  if (P.noise_vec && nv >= 8) {
+                    const float4 v0 = __ldg(reinterpret_cast<const float4*>(nz));
+                    const float4 v1 = __ldg(reinterpret_cast<const float4*>(nz) + 1);
+                    E[0] = v0.x; E[1] = v0.y; E[2] = v0.z; E[3] = v0.w;
+                    E[4] = v1.x; E[5] = v1.y; E[6] = v1.z; E[7] = v1.w;
+                  } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) E[i] = i < nv ? __ldg(nz + i) : INFINITY;
+                  }
+                  float e = gEmin[k][tt];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) e = fminf(e, E[i]);
+                  gEmin[k][tt] = e;
+                }
+              }
+            }
+          }
+        }
+        // unit max: warp reduction, one shared atomic per item
+        const float im = fmaxf(gmax[k][0], gmax[k][1]);
+        const unsigned int key = __reduce_max_sync(0xffffffffu, ordered_key(isnan(im) ? -INFINITY : im));
+        if (lane == 0) atomicMax(&ms.umaxkey[u], key);
+      }
+    }
+    if (__any_sync(0xffffffffu, lnan) && lane == 0) ms.nan = 1;
+    __syncthreads();
+    const bool cnan = ms.nan != 0;
+    float umax[2] = {key_to_float(ms.umaxkey[0]), key_to_float(ms.umaxkey[1])};
+    if (ms.umaxkey[0] == 0u) umax[0] = -INFINITY;
+    if (ms.umaxkey[1] == 0u) umax[1] = -INFINITY;
+    const float cmax = fmaxf(umax[0], umax[1]);
+
+    // greedy: first id holding the CTA max (NaN first if any)
+#pragma unroll
+    for (int k = 0; k < kMaxItems; ++k) {
+      const int item = warp + k * NW;
+      if (item < geo.nitems) {
+        int u, p;
+        item_of(geo, item, u, p);
+        const Unit un = unit_of(geo, u);
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const float gm = gmax[k][tt];
+          const bool scan = cnan || (gm == cmax && n_cta > 0);
+          if (scan) {
+            const int t = 2 * p + tt;
+            const int lg = t * 32 + lane;
+            for (int m = 0; m < 32; ++m) {
+              const int local = int(member_offset(lg, m));
+              if (local >= un.L) continue;
+              const float x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
+              if (cnan ? (x != x) : (x == cmax)) {
+                atomicMin(&ms.gmin, (unsigned int)(geo.cta_start + un.uoff + local));
+                break;
+              }
+            }
+          }
+        }
+      }
+    }
+
+    // small top-k: per-warp top-8 group maxima -> CTA lower bound of the k-th largest
+    if (small_k) {
+      uint32_t keys[kMaxItems * 2];
+#pragma unroll
+      for (int k = 0; k < kMaxItems; ++k)
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const float gm = gmax[k][tt];
+          keys[k * 2 + tt] = (gm > -INFINITY && !isnan(gm)) ? ordered_key(gm) : 0u;
+        }
+      for (int round = 0; round < 8; ++round) {
+        uint32_t lb = 0;
+#pragma unroll
+        for (int i = 0; i < kMaxItems * 2; ++i) lb = max(lb, keys[i]);
+        const uint32_t m = __reduce_max_sync(0xffffffffu, lb);
+        if (lane == 0) ms.wtop[warp * 8 + round] = m;
+        const uint32_t who = __ballot_sync(0xffffffffu, lb == m && m != 0u);
+        if (who && lane == ctz_lane(who)) {
+#pragma unroll
+          for (int i = 0; i < kMaxItems * 2; ++i)
+            if (keys[i] == m) { keys[i] = 0u; break; }
+        }
+      }
+    }
+    __syncthreads();
+    uint32_t topk_lkey = 0u;
+    if (small_k && warp == 0) {
+      // k-th largest of the NW*8 warp maxima (bisection on the ordered key)
+      uint32_t v[NW * 8 / 32];
+#pragma unroll
+      for (int i = 0; i < NW * 8 / 32; ++i) v[i] = ms.wtop[lane + 32 * i];
+      uint32_t L = 0;
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t tryk = L | (1u << bit);
+        int c = 0;
+#pragma unroll
+        for (int i = 0; i < NW * 8 / 32; ++i) c += __popc(__ballot_sync(0xffffffffu, v[i] >= tryk));
+        if (c >= kk) L = tryk;
+      }
+      topk_lkey = L;
+    }
+
+    // ------------------------------------------------------------ race (local, CTA scale)
+    const float c0 = max_coef(cmax, c1);
+    const bool race_ok = need_race && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY;
+    const int Rr = !(p_on || k_on) ? 1 : (p_on && !k_on ? (tp >= 0.9f ? 2 : (tp >= 0.75f ? 3 : 4)) : 4);
+    if (lane == 0) {
+      for (int i = 0; i < kMaxR; ++i) wl[i] = Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
+    }
+    __syncwarp();
+    NoiseKey nkey;
+    NoiseRoot root{0.f, 0};
+    int64_t gid_s = -1;
+    int mem_s = 0;
+    if (race_ok) {
+      const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+      nkey = make_noise_key(a.seed, step, a.row_offset + row);
+      if (!a.noise) {
+        root = noise_root(nkey, V);
+        token_group(root.s, V, &gid_s, &mem_s);
+      }
+    }
+    float bound[kMaxItems][2];
+    int garg[kMaxItems][2];
+    bool done_g[kMaxItems][2];
+#pragma unroll
+    for (int k = 0; k < kMaxItems; ++k)
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) { bound[k][tt] = -1.f; garg[k][tt] = 0; done_g[k][tt] = false; }
+    if (race_ok) {
+#pragma unroll
+      for (int k = 0; k < kMaxItems; ++k) {
+        const int item = warp + k * NW;
+        if (item < geo.nitems) {
+          int u, p;
+          item_of(geo, item, u, p);
+          const Unit un = unit_of(geo, u);
+          const uint32_t ctr = uint32_t(un.pbase + p * 32 + lane);
+          U4 w{0, 0, 0, 0};
+          if (!a.noise) w = philox_at(nkey, ctr, kTagGroup);
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * p + tt;
+            const int lg = t * 32 + lane;
+            const int n = t < un.ntiles ? group_size(lg, un.L) : 0;
+            if (n > 0 && gmax[k][tt] > -INFINITY) {
+              float emin;
+              if (a.noise) {
+                emin = gEmin[k][tt];
+              } else {
+                const int64_t gid = un.gbase + lg;
+                if (gid == gid_s) { emin = root.e_root; garg[k][tt] = mem_s; }
+                else {
+                  const GroupMin gmn = tt ? group_min_from(root, w.z, w.w, n) : group_min_from(root, w.x, w.y, n);
+                  emin = gmn.e_min; garg[k][tt] = gmn.arg;
+                }
+              }
+              gEmin[k][tt] = emin;
+              bound[k][tt] = __fdividef(unnorm(gmax[k][tt], c1, c0), emin);
+            }
+          }
+        }
+      }
+    }
+    // warp-cooperative evaluation of one group (owner lane ol, item k, tile parity tt)
+    auto eval_group = [&](int k, int tt, int ol) {
+      const int item = warp + k * NW;
+      int u, p;
+      item_of(geo, item, u, p);
+      const Unit un = unit_of(geo, u);
+      const int t = 2 * p + tt;
+      const int lg = t * 32 + ol;
+      float em_own = 0.f;
+      int ag_own = 0;
+#pragma unroll
+      for (int kq = 0; kq < kMaxItems; ++kq)
+#pragma unroll
+        for (int tq = 0; tq < 2; ++tq)
+          if (kq == k && tq == tt) { em_own = gEmin[kq][tq]; ag_own = garg[kq][tq]; }
+      const float emin = __shfl_sync(0xffffffffu, em_own, ol);
+      const int arg = __shfl_sync(0xffffffffu, ag_own, ol);
+      const int local = int(member_offset(lg, lane));
+      float r = -INFINITY, x = 0.f, E = 1.f;
+      int id = 0x7FFFFFFF;
+      if (local < un.L) {
+        x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
+        id = int(geo.cta_start + un.uoff + local);
+        if (a.noise) E = __ldg(a.noise + row * a.noise_ld + id);
+        else E = lane == arg ? emin : __fadd_rn(emin, neglog(uniform_open([&] {
+                   const U4 tw = philox_at(nkey, uint32_t(id >> 2), kTagToken);
+                   const int s = id & 3;
+                   return s == 0 ? tw.x : s == 1 ? tw.y : s == 2 ? tw.z : tw.w;
+                 }())));
+        r = __fdiv_rn(unnorm(x, c1, c0), E);
+        if (r != r) r = -INFINITY;
+      }
+      warp_merge(wl, Rr, r, x, E, id);
+    };
+    if (race_ok) {
+      // R1: each warp expands its best-bound group
+      float bb = -1.f; int bk = 0, btt = 0;
+#pragma unroll
+      for (int k = 0; k < kMaxItems; ++k)
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt)
+          if (bound[k][tt] > bb) { bb = bound[k][tt]; bk = k; btt = tt; }
+      float wb = bb; int wlane = lane;
+      for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, wb, o);
+        const int ol = __shfl_xor_sync(0xffffffffu, wlane, o);
+        if (ob > wb || (ob == wb && ol < wlane)) { wb = ob; wlane = ol; }
+      }
+      if (wb > 0.f) {
+        const int k = __shfl_sync(0xffffffffu, bk, wlane), tt = __shfl_sync(0xffffffffu, btt, wlane);
+        if (lane == wlane) {
+#pragma unroll
+          for (int kq = 0; kq < kMaxItems; ++kq)
+#pragma unroll
+            for (int tq = 0; tq < 2; ++tq)
+              if (kq == k && tq == tt) done_g[kq][tq] = true;
+        }
+        eval_group(k, tt, wlane);
+      }
+    }
+    __syncthreads();
+    if (race_ok && warp == 0) {
+      // CTA threshold: the Rr-th best ratio over all warp lists
+      float v[NW * kMaxR / 32 > 0 ? (NW * kMaxR + 31) / 32 : 1];
+      constexpr int PER = (NW * kMaxR + 31) / 32;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int idx = lane + 32 * i;
+        v[i] = (idx < NW * kMaxR && (idx % kMaxR) < Rr) ? wl_all[idx].r : -INFINITY;
+      }
+      float th = -INFINITY;
+      for (int round = 0; round < Rr; ++round) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) m = fmaxf(m, v[i]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        th = m;
+        const uint32_t who = __ballot_sync(0xffffffffu, [&] {
+          bool h = false;
+#pragma unroll
+          for (int i = 0; i < PER; ++i) h |= (v[i] == m);
+          return h;
+        }());
+        if (who && lane == ctz_lane(who)) {
+#pragma unroll
+          for (int i = 0; i < PER; ++i) if (v[i] == m) { v[i] = -INFINITY; break; }
+        }
+      }
+      if (lane == 0) ms.theta = th > -INFINITY ? th : 0.f;
+    }
+    __syncthreads();
+    if (race_ok) {
+      // R2: expand every group whose bound can still reach the threshold
+      float theta = ms.theta;
+      for (;;) {
+        bool any = false;
+        int fk = 0, ftt = 0;
+#pragma unroll
+        for (int k = 0; k < kMaxItems; ++k)
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt)
+            if (!any && !done_g[k][tt] && bound[k][tt] > 0.f && bound[k][tt] >= theta * 0.99998f) {
+              any = true; fk = k; ftt = tt;
+            }
+        const uint32_t who = __ballot_sync(0xffffffffu, any);
+        if (!who) break;
+        const int ol = ctz_lane(who);
+        const int k = __shfl_sync(0xffffffffu, fk, ol), tt = __shfl_sync(0xffffffffu, ftt, ol);
+        if (lane == ol) {
+#pragma unroll
+          for (int kq = 0; kq < kMaxItems; ++kq)
+#pragma unroll
+            for (int tq = 0; tq < 2; ++tq)
+              if (kq == k && tq == tt) done_g[kq][tq] = true;
+        }
+        eval_group(k, tt, ol);
+        __syncwarp();
+        theta = fmaxf(theta, wl[Rr - 1].r);
+      }
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------ exchange 1
+    Share& my = share[ex & 1];
+    if (warp == 0) {
+      // CTA top-Rr from the warp lists
+      constexpr int PER = (NW * kMaxR + 31) / 32;
+      Cand c[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int idx = lane + 32 * i;
+        c[i] = (race_ok && idx < NW * kMaxR && (idx % kMaxR) < Rr) ? wl_all[idx] : Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
+      }
+      int n = 0;
+      for (int round = 0; round < Rr; ++round) {
+        int bi = 0;
+#pragma unroll
+        for (int i = 1; i < PER; ++i) if (rbetter(c[i].r, c[i].id, c[bi].r, c[bi].id)) bi = i;
+        float br = c[bi].r; int bid = c[bi].id; int bl = lane;
+        for (int o = 16; o; o >>= 1) {
+          const float orr = __shfl_xor_sync(0xffffffffu, br, o);
+          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+          const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+          if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; bl = ol; }
+        }
+        if (!(br > -INFINITY)) break;
+        if (lane == bl) { my.cand[n] = c[bi]; c[bi].r = -INFINITY; c[bi].id = 0x7FFFFFFF; }
+        ++n;
+      }
+      if (lane == 0) {
+        my.ncand = n;
+        my.umax[0] = umax[0]; my.umax[1] = umax[1];
+        my.cmax = cnan ? NAN : cmax;
+        my.c0 = c0;
+        my.nan = cnan ? 1 : 0;
+        my.gidx = int(ms.gmin == 0xFFFFFFFFu ? 0x7FFFFFFF : ms.gmin);
+        my.gval = cnan ? NAN : cmax;
+        my.topk_lkey = topk_lkey;
+      }
+    }
+    cluster.sync();
+    if (threadIdx.x == 0) {
+      // every CTA computes the same row state from the same shares
+      float xM = -INFINITY; bool nan = false; float gv = -INFINITY; int gi = 0x7FFFFFFF;
+      uint32_t lkey = 0u;
+      for (int r = 0; r < CL; ++r) {
+        const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
+        nan |= s->nan != 0;
+        if (s->gidx != 0x7FFFFFFF && argmax_better(s->gval, s->gidx, gv, gi)) { gv = s->gval; gi = s->gidx; }
+        for (int u = 0; u < U; ++u) {
+          rs.umax[r * U + u] = s->umax[u];
+          xM = fmaxf(xM, s->umax[u]);
+        }
+        lkey = max(lkey, s->topk_lkey);
+      }
+      const float nM = max_coef(xM, c1);
+      rs.xM = xM; rs.nM = nM; rs.c1 = c1;
+      rs.p_on = p_on; rs.k_on = k_on; rs.k = kk; rs.tp = tp;
+      rs.L = lkey ? key_to_float(lkey) : -INFINITY;
+      const bool nonfinite = nan || !(xM > -INFINITY) || xM == INFINITY || (!greedy && !(fabsf(nM) < INFINITY));
+      rs.status = greedy ? QE_ROW_GREEDY : (nonfinite ? QE_ROW_NONFINITE : 0);
+      rs.out = gi == 0x7FFFFFFF ? 0 : gi;
+      if (greedy || nonfinite || (k_on && kk == 1)) {
+        rs.type = kDone;
+      } else if (small_k) {
+        rs.type = kGather;
+      } else {
+        // merge the CTA candidate lists (scaled to the row max)
+        int n = 0;
+        Cand best[kMaxR];
+        double bestr[kMaxR];
+        for (int r = 0; r < CL; ++r) {
+          const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
+          const double sc = exp2(double(nM) - double(s->c0));
+          for (int i = 0; i < s->ncand; ++i) {
+            Cand c = s->cand[i];
+            const double rv = double(c.r) * sc;
+            int j = n < Rr ? n : Rr - 1;
+            if (n >= Rr && !(rv > bestr[Rr - 1] || (rv == bestr[Rr - 1] && c.id < best[Rr - 1].id))) continue;
+            while (j > 0 && (rv > bestr[j - 1] || (rv == bestr[j - 1] && c.id < best[j - 1].id))) {
+              best[j] = best[j - 1]; bestr[j] = bestr[j - 1]; --j;
+            }
+            best[j] = c; bestr[j] = rv;
+            if (n < Rr) ++n;
+          }
+        }
+        for (int i = 0; i < n; ++i) rs.cand[i] = best[i];
+        rs.R = n;
+        if (n == 0) {
+          rs.type = kDone;  // nothing finite to race: keep the greedy choice
+          rs.status = QE_ROW_NONFINITE;
+        } else if (!p_on && !k_on) {
+          rs.type = kDone;
+          rs.out = best[0].id;
+        } else {
+          rs.type = kRaceTest;
+        }
+      }
+    }
+    ++ex;
+    __syncthreads();
+
+    if (rs.type == kDone) {
+      if (q == 0 && threadIdx.x == 0) {
+        a.out_ids[row] = rs.out;
+        if (a.out_status) a.out_status[row] = rs.status;
+      }
+      __syncthreads();
+      continue;
+    }
+
+    // ------------------------------------------------------------ pass B
+    const float nM = rs.nM;
+    const int R = rs.type == kRaceTest ? rs.R : 0;
+    const float Lg = rs.L;
+    float cv[kMaxR];
+    int cid_[kMaxR];
+#pragma unroll
+    for (int c = 0; c < kMaxR; ++c) { cv[c] = c < R ? rs.cand[c].x : 0.f; cid_[c] = c < R ? rs.cand[c].id : 0; }
+    float Fl[kMaxR];
+    long long Cl[kMaxR];
+#pragma unroll
+    for (int c = 0; c < kMaxR; ++c) { Fl[c] = 0.f; Cl[c] = 0; }
+    unsigned long long sfx[2] = {0ull, 0ull};
+    const bool gather_row = rs.type == kGather;
+#pragma unroll
+    for (int k = 0; k < kMaxItems; ++k) {
+      const int item = warp + k * NW;
+      if (item < geo.nitems) {
+        int u, p;
+        item_of(geo, item, u, p);
+        const Unit un = unit_of(geo, u);
+        const float um = u ? umax[1] : umax[0];
+        const float c0u = max_coef(um, c1);
+        const bool uok = um > -INFINITY;
+        const float scale = uok ? exp2f(nM - c0u) : 0.f;
+        // candidate thresholds for this unit: x > th (GE via the float below v)
+        float th[kMaxR];
+        bool mixed[kMaxR];
+#pragma unroll
+        for (int c = 0; c < kMaxR; ++c) {
+          mixed[c] = c < R && cid_[c] >= un.ustart && cid_[c] < un.uend;
+          th[c] = (c < R && cid_[c] >= un.uend) ? nextafterf(cv[c], -INFINITY) : cv[c];
+        }
+        float Fi[kMaxR];
+        long long Ci[kMaxR];
+#pragma unroll
+        for (int c = 0; c < kMaxR; ++c) { Fi[c] = 0.f; Ci[c] = 0; }
+        unsigned long long sfu = 0ull;
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * p + tt;
+          float fs = 0.f;
+          if (t < un.ntiles && uok) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int local = t * kTile + b * 256 + lane * 8;
+              const int nv = max(0, min(8, un.L - local));
+              const int off = un.uoff + local;
+              float x[8];
+              Load8<T>::run(data, off, nv, x);
+              if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float e = unnorm(x[i], c1, c0u);
+                fs = __fadd_rn(fs, e);
+#pragma unroll
+                for (int c = 0; c < kMaxR; ++c) {
+                  if (c < R) {
+                    bool pred = x[i] > th[c];
+                    if (mixed[c]) pred = pred || (x[i] == cv[c] && int(geo.cta_start + off + i) < cid_[c]);
+                    if (pred) { Fi[c] += e; Ci[c] += 1; }
+                  }
+                }
+              }
+              if (gather_row) {
+                unsigned mask = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mask |= ((i < nv && x[i] >= Lg) ? 1u : 0u) << i;
+                gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
+              }
+            }
+          }
+          if (fs > 0.f) sfu += __double2ull_rn(double(fs) * kSumScale);
+        }
+        if (u) sfx[1] += sfu; else sfx[0] += sfu;
+#pragma unroll
+        for (int c = 0; c < kMaxR; ++c) { Fl[c] += Fi[c] * scale; Cl[c] += Ci[c]; }
+      }
+    }
+    // reductions: warp -> shared -> thread 0
+#pragma unroll
+    for (int c = 0; c < kMaxR; ++c) {
+      if (c < R) {
+        float f = Fl[c];
+        long long n = Cl[c];
+        for (int o = 16; o; o >>= 1) {
+          f += __shfl_xor_sync(0xffffffffu, f, o);
+          n += __shfl_xor_sync(0xffffffffu, n, o);
+        }
+        if (lane == 0) { ms.wF[warp][c] = f; ms.wcnt[warp][c] = n; }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      unsigned long long s = sfx[u];
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) ms.wsfix[warp][u] = s;
+    }
+    __syncthreads();
+    Share& my2 = share[ex & 1];
+    if (threadIdx.x == 0) {
+      for (int u = 0; u < 2; ++u) {
+        unsigned long long s = 0;
+        for (int w = 0; w < NW; ++w) s += ms.wsfix[w][u];
+        my2.sfix[u] = s;
+      }
+      for (int c = 0; c < R; ++c) {
+        double f = 0.0; long long n = 0;
+        for (int w = 0; w < NW; ++w) { f += double(ms.wF[w][c]); n += ms.wcnt[w][c]; }
+        my2.F[c] = f; my2.cnt[c] = n;
+      }
+      my2.ngather = ms.ngather;
+      my2.overflow = ms.ngather > kGatherCap ? 1 : 0;
+    }
+    cluster.sync();
+    if (threadIdx.x == 0) {
+      double Sd = 0.0;
+      double F[kMaxR];
+      long long C[kMaxR];
+      for (int c = 0; c < kMaxR; ++c) { F[c] = 0.0; C[c] = 0; }
+      int ngat = 0, ovf = 0;
+      for (int r = 0; r < CL; ++r) {
+        const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
+        for (int u = 0; u < U; ++u) {
+          const float um = rs.umax[r * U + u];
+          if (um > -INFINITY) Sd += double(s->sfix[u]) * (1.0 / kSumScale) * exp2(double(nM) - double(max_coef(um, c1)));
+        }
+        for (int c = 0; c < R; ++c) { F[c] += s->F[c]; C[c] += s->cnt[c]; }
+        ngat += s->ngather;
+        ovf |= s->overflow;
+      }
+      rs.S = Sd;
+      rs.Sf = float(Sd);
+      if (!(rs.Sf > 0.f) || rs.Sf == INFINITY) {
+        rs.type = kDone;
+        rs.status = QE_ROW_NONFINITE;
+      } else if (rs.type == kRaceTest) {
+        // exact ratios, then the first candidate inside the kept set
+        int order[kMaxR];
+        for (int c = 0; c < R; ++c) {
+          const float p = __fdiv_rn(unnorm(rs.cand[c].x, c1, nM), rs.Sf);
+          rs.rM[c] = __fdiv_rn(p, rs.cand[c].E);
+          order[c] = c;
+        }
+        for (int i = 1; i < R; ++i) {
+          const int v = order[i];
+          int j = i;
+          while (j > 0 && rbetter(rs.rM[v], rs.cand[v].id, rs.rM[order[j - 1]], rs.cand[order[j - 1]].id)) {
+            order[j] = order[j - 1]; --j;
+          }
+          order[j] = v;
+        }
+        int win = -1;
+        float Lx = -INFINITY;
+        for (int i = 0; i < R; ++i) {
+          const int c = order[i];
+          const bool okp = !p_on || F[c] <= double(tp) * Sd;
+          const bool okk = !k_on || C[c] < kk;
+          if (okp && okk) { win = c; break; }
+          Lx = fmaxf(Lx, rs.cand[c].x);
+        }
+        if (win >= 0) {
+          rs.type = kDone;
+          rs.out = rs.cand[win].id;
+        } else {
+          rs.type = kGather;  // every kept token is >= the best rejected candidate
+          rs.L = Lx;
+        }
+      } else {
+        if (ovf || ngat > P.merge_cap) rs.type = kSlow;
+      }
+      rs.R = ngat;
+    }
+    ++ex;
+    __syncthreads();
+    if (rs.type == kDone) {
+      if (q == 0 && threadIdx.x == 0) {
+        a.out_ids[row] = rs.out;
+        if (a.out_status) a.out_status[row] = rs.status;
+      }
+      __syncthreads();
+      continue;
+    }
+    if (rs.type == kGather && R > 0) {
+      // pass C: gather the keys of every token >= L (no exponentials)
+      if (threadIdx.x == 0) ms.ngather = 0;
+      __syncthreads();
+      const float Lc = rs.L;
+#pragma unroll
+      for (int k = 0; k < kMaxItems; ++k) {
+        const int item = warp + k * NW;
+        if (item < geo.nitems) {
+          int u, p;
+          item_of(geo, item, u, p);
+          const Unit un = unit_of(geo, u);
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * p + tt;
+            if (t < un.ntiles) {
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const int local = t * kTile + b * 256 + lane * 8;
+                const int nv = max(0, min(8, un.L - local));
+                const int off = un.uoff + local;
+                float x[8];
+                Load8<T>::run(data, off, nv, x);
+                if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+                unsigned mask = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mask |= ((i < nv && x[i] >= Lc) ? 1u : 0u) << i;
+                gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();
+      Share& my3 = share[ex & 1];
+      if (threadIdx.x == 0) {
+        my3.ngather = ms.ngather;
+        my3.overflow = ms.ngather > kGatherCap ? 1 : 0;
+      }
+      cluster.sync();
+      if (threadIdx.x == 0) {
+        int ngat = 0, ovf = 0;
+        for (int r = 0; r < CL; ++r) {
+          const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
+          ngat += s->ngather;
+          ovf |= s->overflow;
+        }
+        rs.R = ngat;
+        if (ovf || ngat > P.merge_cap) rs.type = kSlow;
+      }
+      ++ex;
+      __syncthreads();
+    }
+
+    if (rs.type == kGather) {
+      // CTA 0 finishes the row exactly from the gathered keys; the others move on
+      if (q == 0) {
+        unsigned long long* keys = reinterpret_cast<unsigned long long*>(data);
+        const int n = rs.R;
+        int np2 = 1;
+        while (np2 < n) np2 <<= 1;
+        // copy every CTA's list (their lists stay intact until CTA 0 joins the next exchange)
+        int base = 0;
+        for (int r = 0; r < CL; ++r) {
+          const Share* s = cluster.map_shared_rank(&share[(ex - 1) & 1], r);
+          const int cnt = s->ngather;
+          const unsigned long long* src = cluster.map_shared_rank(gath, r);
+          for (int i = threadIdx.x; i < cnt; i += NT) keys[base + i] = src[i];
+          base += cnt;
+        }
+        for (int i = n + threadIdx.x; i < np2; i += NT) keys[i] = 0ull;
+        __syncthreads();
+        bitonic_desc<NT>(keys, np2);
+        // probabilities and exclusive prefix mass (block scan in double)
+        double* pm = reinterpret_cast<double*>(gath);  // reuse: own gather list already copied
+        __syncthreads();
+        const float Sf = rs.Sf;
+        const double Sd = rs.S;
+        // each thread handles a contiguous chunk of the sorted keys
+        const int per = (n + NT - 1) / NT;
+        const int i0 = threadIdx.x * per;
+        double local = 0.0;
+        for (int i = i0; i < i0 + per && i < n; ++i) {
+          const float x = key_to_float(uint32_t(keys[i] >> 32));
+          local += double(__fdiv_rn(unnorm(x, c1, nM), Sf));
+        }
+        // block exclusive scan of `local`
+        double incl = local;
+        for (int o = 1; o < 32; o <<= 1) {
+          const double v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        double* wsum = reinterpret_cast<double*>(ms.wF);
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        double woff = 0.0;
+        for (int w = 0; w < warp; ++w) woff += wsum[w];
+        double run = woff + incl - local;
+        // kept prefix: excl(i) <= top_p and i < k; count kept in each chunk
+        int kept = 0;
+        for (int i = i0; i < i0 + per && i < n; ++i) {
+          const float x = key_to_float(uint32_t(keys[i] >> 32));
+          const double pv = double(__fdiv_rn(unnorm(x, c1, nM), Sf));
+          const bool ok = (!p_on || run <= double(tp)) && (!k_on || i < kk);
+          if (!ok) break;
+          ++kept;
+          run += pv;
+        }
+        (void)pm; (void)Sd;
+        // n_K = number of leading kept (kept set is a prefix; chunks are contiguous)
+        __syncthreads();
+        int* kc = reinterpret_cast<int*>(ms.wcnt);
+        // first chunk that is not complete decides the prefix
+        const bool complete = kept == max(0, min(per, n - i0));
+        const unsigned bal = __ballot_sync(0xffffffffu, !complete);
+        if (lane == 0) kc[warp] = bal ? (warp * 32 + ctz_lane(bal)) : 0x7FFFFFFF;
+        __syncthreads();
+        int first_incomplete = 0x7FFFFFFF;
+        for (int w = 0; w < NW; ++w) first_incomplete = min(first_incomplete, kc[w]);
+        __shared__ int s_nk;
+        if (int(threadIdx.x) == first_incomplete) s_nk = i0 + kept;
+        if (threadIdx.x == 0 && first_incomplete == 0x7FFFFFFF) s_nk = n;
+        __syncthreads();
+        const int nK = max(1, min(s_nk, n));
+        // race among the kept tokens
+        const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+        const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
+        NoiseRoot rt{0.f, 0};
+        int64_t gs = -1;
+        int ms_ = 0;
+        if (!a.noise) {
+          rt = noise_root(key, V);
+          token_group(rt.s, V, &gs, &ms_);
+        }
+        float br = -INFINITY;
+        int bid = 0x7FFFFFFF;
+        for (int i = threadIdx.x; i < nK; i += NT) {
+          const float x = key_to_float(uint32_t(keys[i] >> 32));
+          const int id = int(0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFu));
+          const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
+          const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + id) : tree_noise(key, rt, gs, ms_, id, V);
+          const float r = __fdiv_rn(pv, E);
+          if (rbetter(r, id, br, bid)) { br = r; bid = id; }
+        }
+        for (int o = 16; o; o >>= 1) {
+          const float orr = __shfl_xor_sync(0xffffffffu, br, o);
+          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+          if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; }
+        }
+        float* wr = reinterpret_cast<float*>(ms.wsfix);
+        int* wi = reinterpret_cast<int*>(ms.wsfix) + NW;
+        if (lane == 0) { wr[warp] = br; wi[warp] = bid; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
+          a.out_ids[row] = bid == 0x7FFFFFFF ? (nK > 0 ? int(0xFFFFFFFFu - uint32_t(keys[0] & 0xFFFFFFFFu)) : 0) : bid;
+          if (a.out_status) a.out_status[row] = 0;
+        }
+      }
+      __syncthreads();
+      continue;
+    }
+
+    // kSlow: CTA 0 finishes the row over DSMEM; the peers keep their slices
+    // in place until it is done
+    if (q == 0) slow_exact<T, CL>(P, row, cluster, data, pen, gath, rs, use_pen, rpv, ms.slow_int);
+    cluster.sync();
+  }
+  // do not leave while peers may still read this CTA's shared memory
+  cluster.sync();
+  if (threadIdx.x == 0 && ms.err) atomicExch(a.ws.err, 1);
+}
+
+// ---------------------------------------------------------------- host launch
+template <typename T, int CL>
+static int launch_cfg(const KernelArgs& ka, cudaStream_t st, int cap) {
+  using SM = Smem<T, CL>;
+  constexpr int NT = Cfg<CL>::NT;
+  const size_t smem = SM::total(cap);
+  static int configured_cap = -1;
+  static int max_clusters = 0;
+  auto kern = fused_kernel<T, CL>;
+  if (configured_cap != cap) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e == cudaSuccess && CL > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("fused: cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) return set_error(QE_ERR_CUDA, std::string("fused: occupancy query failed: ") + cudaGetErrorString(e));
+    max_clusters = n;
+    configured_cap = cap;
+  }
+  FusedParams P;
+  P.a = ka;
+  P.cap = cap;
+  const uintptr_t base = reinterpret_cast<uintptr_t>(ka.logits);
+  P.tma_ok = (base % 16 == 0) && ((ka.ld * int64_t(sizeof(T))) % 16 == 0);
+  P.noise_vec = ka.noise && (reinterpret_cast<uintptr_t>(ka.noise) % 16 == 0) && (ka.noise_ld % 4 == 0);
+  int mc = 1;
+  while (size_t(mc) * 2 * 8 <= size_t(cap) * sizeof(T)) mc *= 2;
+  P.merge_cap = mc;
+  const int ncl = int(ka.batch < max_clusters ? ka.batch : max_clusters);
+  P.nclusters = ncl;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(ncl * CL));
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr; cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("fused launch: ") + cudaGetErrorString(e));
+  return QE_OK;
+}
+
+}  // namespace fz
+
+// Capacity (elements per CTA) the fused path needs for V, or 0 if unsupported.
+int fused_capacity(int64_t V, int cluster) {
+  const int U = 16 / cluster;
+  int64_t mx = 0;
+  for (int q = 0; q < cluster; ++q) {
+    const int64_t n = slice_start(q * U + U, V) - slice_start(q * U, V);
+    if (n > mx) mx = n;
+  }
+  int64_t cap = ((mx + 1023) / 1024) * 1024 + 1024;
+  if (cap < 8192) cap = 8192;  // room for CTA 0 to sort >= 1024 gathered keys
+  const int NW = cluster == 8 ? 16 : 8;
+  // every warp owns at most kMaxItems tile pairs
+  for (int q = 0; q < cluster; ++q) {
+    int items = 0;
+    for (int u = 0; u < U; ++u) {
+      const int64_t L = slice_start(q * U + u + 1, V) - slice_start(q * U + u, V);
+      items += int(((L + kTile - 1) / kTile + 1) / 2);
+    }
+    if (items > fz::kMaxItems * NW) return 0;
+  }
+  return int(cap);
+}
+
+int launch_fused(const KernelArgs& ka, cudaStream_t st, int cluster) {
+  const int cap = fused_capacity(ka.vocab, cluster);
+  if (!cap) return set_error(QE_ERR_UNSUPPORTED, "fused path: vocab too large");
+  if (cluster == 16) {
+    switch (ka.dtype) {
+      case QE_DTYPE_F32: return fz::launch_cfg<float, 16>(ka, st, cap);
+      case QE_DTYPE_BF16: return fz::launch_cfg<__nv_bfloat16, 16>(ka, st, cap);
+      case QE_DTYPE_F16: return fz::launch_cfg<__half, 16>(ka, st, cap);
+    }
+  } else {
+    switch (ka.dtype) {
+      case QE_DTYPE_F32: return fz::launch_cfg<float, 8>(ka, st, cap);
+      case QE_DTYPE_BF16: return fz::launch_cfg<__nv_bfloat16, 8>(ka, st, cap);
+      case QE_DTYPE_F16: return fz::launch_cfg<__half, 8>(ka, st, cap);
+    }
+  }
+  return set_error(QE_ERR_INVALID, "unknown dtype");
+}
+
+}  // namespace qe

@@ -20,10 +20,18 @@ pytestmark = pytest.mark.gpu
 CASES = C.build_cases()
 
 
-@pytest.fixture(scope="module")
-def sampler():
+@pytest.fixture(scope="module", params=["fused", "ref"])
+def sampler(request):
+    """Both kernel paths: the fused cluster kernel and the multi-kernel one."""
+    import os
     from qedge_b200.sampler import QESampler
-    return QESampler(seed=0)
+    old = os.environ.get("QE_SAMPLER_PATH")
+    os.environ["QE_SAMPLER_PATH"] = request.param
+    yield QESampler(seed=0)
+    if old is None:
+        os.environ.pop("QE_SAMPLER_PATH", None)
+    else:
+        os.environ["QE_SAMPLER_PATH"] = old
 
 
 @pytest.mark.parametrize("name", sorted(CASES))
