@@ -46,7 +46,9 @@ enum qe_status {
 /* per-row status bits written to out_status (when non-NULL) */
 enum qe_row_status {
   QE_ROW_GREEDY = 1,       /* row sampled as greedy argmax (T <= 1e-5 or all_greedy) */
-  QE_ROW_NONFINITE = 2     /* probabilities not finite; greedy argmax returned */
+  QE_ROW_NONFINITE = 2,    /* probabilities not finite; greedy argmax returned */
+  QE_ROW_GATHERED = 4,     /* diagnostic: finished from the gathered head of the row */
+  QE_ROW_SLOW = 8          /* diagnostic: finished by the single-CTA exact fallback */
 };
 
 typedef struct qe_sample_args {

@@ -14,7 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqesample.so"
 QE_ABI_VERSION = 1
 QE_DTYPE_F32, QE_DTYPE_BF16, QE_DTYPE_F16 = 0, 1, 2
 QE_FLAG_ALL_GREEDY, QE_FLAG_USE_TOP_P = 1, 2
-QE_ROW_GREEDY, QE_ROW_NONFINITE = 1, 2
+QE_ROW_GREEDY, QE_ROW_NONFINITE, QE_ROW_GATHERED, QE_ROW_SLOW = 1, 2, 4, 8
 STATUS_NAMES = {0: "QE_OK", -1: "QE_ERR_INVALID", -2: "QE_ERR_CUDA",
                 -3: "QE_ERR_WORKSPACE", -4: "QE_ERR_UNSUPPORTED"}
 

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <string>
 
+#include "qe_common.cuh"
 #include "qe_internal.h"
 
 namespace qe {
@@ -19,9 +20,15 @@ int set_error(int code, const std::string& msg) {
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-size_t workspace_bytes(int64_t batch) {
+int64_t groups_per_row(int64_t vocab) {
+  int64_t n = 0;
+  for (int g = 0; g < kNumSlices; ++g) n += slice_groups(slice_start(g + 1, vocab) - slice_start(g, vocab));
+  return n;
+}
+
+size_t workspace_bytes(int64_t batch, int64_t vocab) {
   size_t b = size_t(batch);
-  size_t n = 0;
+  size_t n = align_up(b * size_t(groups_per_row(vocab)) * sizeof(GroupPart), 256);
   n = align_up(n + b * kSlices * sizeof(SlicePart), 256);
   n = align_up(n + b * sizeof(RowInfo), 256);
   n = align_up(n + b * kSlices * sizeof(RacePart), 256);
@@ -29,10 +36,13 @@ size_t workspace_bytes(int64_t batch) {
   return n;
 }
 
-Workspace carve_workspace(void* base, int64_t batch) {
+Workspace carve_workspace(void* base, int64_t batch, int64_t vocab) {
   char* p = static_cast<char*>(base);
   size_t b = size_t(batch), n = 0;
   Workspace w;
+  w.groups = reinterpret_cast<GroupPart*>(p);
+  w.groups_per_row = groups_per_row(vocab);
+  n = align_up(b * size_t(w.groups_per_row) * sizeof(GroupPart), 256);
   w.slices = reinterpret_cast<SlicePart*>(p + n);
   n = align_up(n + b * kSlices * sizeof(SlicePart), 256);
   w.rows = reinterpret_cast<RowInfo*>(p + n);
@@ -52,8 +62,7 @@ extern "C" int qe_abi_version(void) { return QE_ABI_VERSION; }
 extern "C" const char* qe_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" size_t qe_sample_workspace_size(int64_t batch, int64_t vocab) {
-  (void)vocab;
-  return batch > 0 ? workspace_bytes(batch) : 0;
+  return batch > 0 && vocab > 0 ? workspace_bytes(batch, vocab) : 0;
 }
 
 extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
@@ -76,7 +85,7 @@ extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
   const bool pen = a->history && a->rep_penalties;
   if (pen && a->vocab > 48 * 1024 * 32)
     return set_error(QE_ERR_UNSUPPORTED, "repetition penalty supports vocab <= 1,572,864");
-  const size_t need = workspace_bytes(a->batch);
+  const size_t need = workspace_bytes(a->batch, a->vocab);
   if (!a->workspace || a->workspace_bytes < need)
     return set_error(QE_ERR_WORKSPACE, "workspace smaller than qe_sample_workspace_size()");
   if (reinterpret_cast<uintptr_t>(a->workspace) % 256)
@@ -100,7 +109,7 @@ extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
   ka.out_ids = a->out_ids;
   ka.out_probs = a->out_probs; ka.probs_ld = a->probs_ld;
   ka.out_status = a->out_status;
-  ka.ws = carve_workspace(a->workspace, a->batch);
+  ka.ws = carve_workspace(a->workspace, a->batch, a->vocab);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // path choice: the fused cluster kernel unless QE_SAMPLER_PATH=ref, the
   // debug probabilities are requested, or the vocabulary is too large

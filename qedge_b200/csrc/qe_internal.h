@@ -21,6 +21,12 @@ struct alignas(32) SlicePart {
   uint32_t pad;
 };
 
+// Per-group max and group-relative softmax sum (canonical S terms).
+struct GroupPart {
+  float gmax;
+  float fsum;
+};
+
 // Per-row state shared between passes.
 struct alignas(16) RowInfo {
   float M, S;               // M: -RN(xmax * c1) (row exponent offset); S: softmax normaliser
@@ -42,6 +48,8 @@ struct alignas(16) RacePart {
 };
 
 struct Workspace {
+  GroupPart* groups;        // [B, groups_per_row]
+  int64_t groups_per_row;
   SlicePart* slices;
   RowInfo* rows;
   RacePart* race;
@@ -73,8 +81,9 @@ struct KernelArgs {
   Workspace ws;
 };
 
-size_t workspace_bytes(int64_t batch);
-Workspace carve_workspace(void* base, int64_t batch);
+size_t workspace_bytes(int64_t batch, int64_t vocab);
+Workspace carve_workspace(void* base, int64_t batch, int64_t vocab);
+int64_t groups_per_row(int64_t vocab);
 
 int set_error(int code, const std::string& msg);
 int launch_ref_path(const KernelArgs& ka, cudaStream_t st);

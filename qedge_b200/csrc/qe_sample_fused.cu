@@ -7,13 +7,14 @@
 // the 8 (or 16) CTAs of a cluster; CTA q holds canonical vocab slices
 // [qU, qU+U).  Per row:
 //
-//   pass A   group maxima (32 ids per lane group), NaN flags, greedy argmax
+//   pass 1   per 32-id group: max, then the canonical softmax sum relative
+//            to the group max (the only pass with an exponential per token)
 //   race     lazy exponential race: a group's best ratio is bounded by
 //            max(e)/min(E); only groups whose bound can still win are
 //            expanded, using the minimum-first Philox noise tree
 //   exchange candidates over DSMEM (cluster barrier)
-//   pass B   canonical softmax sums and, for the few race candidates, the
-//            exact probability mass and rank of the tokens ahead of them
+//   pass 2   sparse: only groups whose max lies above a candidate are read,
+//            giving the exact probability mass and rank ahead of it
 //   exchange decide: the first candidate (in race order) inside the
 //            top-k / top-p set wins
 //
@@ -25,6 +26,8 @@
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "qe_common.cuh"
@@ -36,8 +39,9 @@ namespace cg = cooperative_groups;
 namespace qe {
 namespace fz {
 
-constexpr int kMaxR = 8;          // race candidates tracked per row
+constexpr int kMaxR = 4;          // race candidates tested per row
 constexpr int kMaxItems = 2;      // tile pairs a warp owns per row
+constexpr int kSlots = 2 * kMaxItems;  // groups per lane
 constexpr int kGatherCap = 1024;  // gathered keys per CTA
 constexpr int kSmallK = 64;       // top-k rows up to this k take the gather path
 constexpr uint32_t kWaitLimit = 1u << 26;
@@ -51,6 +55,7 @@ struct Cand {
   int id;    // token id
 };
 
+// What a CTA publishes to its cluster peers (read over DSMEM).
 struct alignas(16) Share {
   float umax[2];
   float cmax;
@@ -59,14 +64,14 @@ struct alignas(16) Share {
   int ncand;
   int gidx;
   float gval;
-  uint32_t topk_lkey;
+  uint32_t lkey;
   int ngather;
   int overflow;
   int pad;
   Cand cand[kMaxR];
-  unsigned long long sfix[2];
-  double F[kMaxR];
+  unsigned long long sfix;
   long long cnt[kMaxR];
+  double F[kMaxR];
 };
 
 struct RowState {
@@ -79,9 +84,8 @@ struct RowState {
   float c1, nM, xM, Sf;
   double S;
   float L;               // gather lower bound (x' >= L)
-  float umax[16];        // every slice's max (for S)
+  float theta;           // row-scale race threshold from the seeds
   Cand cand[kMaxR];      // global candidates, race order (approximate)
-  float rM[kMaxR];       // their exact ratios once S is known
 };
 
 template <int CL>
@@ -94,10 +98,32 @@ struct Cfg {
 struct FusedParams {
   KernelArgs a;
   int nclusters;
-  int cap;         // data capacity in elements (multiple of 256)
+  int cap;         // data capacity in elements
   int tma_ok;      // logits rows 16-byte aligned
   int noise_vec;   // noise rows 16-byte aligned
   int merge_cap;   // keys CTA 0 can sort in its data buffer (power of two)
+};
+
+struct Misc {
+  uint64_t mbar;
+  unsigned int umaxkey[2];
+  int nan;
+  unsigned int gmin;
+  int err;
+  int ngather;
+  float e_root;
+  int s_mem;
+  long long s_gid;
+  unsigned int wtop[16 * 8];
+  float wb[16];
+  int wbslot[16];
+  float wF[16][kMaxR];
+  long long wcnt[16][kMaxR];
+  unsigned long long wsfix[16];
+  float c0peer[16];
+  long long tstart[17];
+  long long tgbase[16];
+  int slow_int[48];
 };
 
 // ---------------------------------------------------------------- smem layout
@@ -108,32 +134,12 @@ struct Smem {
   static __host__ __device__ size_t pen_off(int cap) { return (data_bytes(cap) + 127) / 128 * 128; }
   static __host__ __device__ size_t gather_off(int cap) { return pen_off(cap) + ((cap / 32 + 1) * 4 + 15) / 16 * 16; }
   static __host__ __device__ size_t share_off(int cap) { return gather_off(cap) + kGatherCap * 8; }
-  static __host__ __device__ size_t wl_off(int cap) { return share_off(cap) + 2 * sizeof(Share); }
+  static __host__ __device__ size_t peer_off(int cap) { return share_off(cap) + 2 * sizeof(Share); }
+  static __host__ __device__ size_t wl_off(int cap) { return peer_off(cap) + size_t(CL) * sizeof(Share); }
   static __host__ __device__ size_t rs_off(int cap) { return wl_off(cap) + size_t(NW) * kMaxR * sizeof(Cand); }
   static __host__ __device__ size_t misc_off(int cap) { return (rs_off(cap) + sizeof(RowState) + 15) / 16 * 16; }
-  static __host__ __device__ size_t total(int cap);
+  static __host__ __device__ size_t total(int cap) { return misc_off(cap) + (sizeof(Misc) + 127) / 128 * 128; }
 };
-
-struct Misc {
-  uint64_t mbar;
-  unsigned int umaxkey[2];
-  int nan;
-  unsigned int gmin;
-  int err;
-  int ngather;
-  int overflow;
-  float theta;
-  unsigned int wtop[16 * 8];
-  float wF[16][kMaxR];
-  long long wcnt[16][kMaxR];
-  unsigned long long wsfix[16][2];
-  int slow_int[48];
-};
-
-template <typename T, int CL>
-__host__ __device__ size_t Smem<T, CL>::total(int cap) {
-  return misc_off(cap) + (sizeof(Misc) + 127) / 128 * 128;
-}
 
 // ---------------------------------------------------------------- small helpers
 __device__ __forceinline__ int ctz_lane(uint32_t m) { return __ffs(m) - 1; }
@@ -300,11 +306,6 @@ __device__ void bitonic_desc(unsigned long long* k, int n) {
   }
 }
 
-template <typename T, int CL>
-struct Kernel {
-  static constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
-  using S = Smem<T, CL>;
-};
 
 // Exact finish of one row by CTA 0 alone, reading every CTA's slice over
 // DSMEM (the peers wait at a cluster barrier meanwhile).  The kept set is
@@ -476,7 +477,107 @@ __device__ void slow_exact(const FusedParams& P, int64_t row, cg::cluster_group&
   if (threadIdx.x == 0) {
     for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
     a.out_ids[row] = bid == 0x7FFFFFFF ? rs.out : bid;
-    if (a.out_status) a.out_status[row] = 0;
+    if (a.out_status) a.out_status[row] = QE_ROW_SLOW;
+  }
+  __syncthreads();
+}
+
+
+// CTA 0 finishes a row from the keys every CTA gathered (all tokens with
+// x' >= L, which provably contains the kept set): sort, exclusive prefix
+// mass, kept prefix, race over the kept tokens.
+template <typename T, int CL>
+__device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg::cluster_group& cluster,
+                                           void* data, unsigned long long* gath, Share* slot,
+                                           const RowState& rs, Misc& ms) {
+  constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW;
+  const KernelArgs& a = P.a;
+  const int64_t V = a.vocab;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(data);
+  const int n = rs.R;
+  int np2 = 1;
+  while (np2 < n) np2 <<= 1;
+  int base = 0;
+  for (int r = 0; r < CL; ++r) {
+    const Share* s = cluster.map_shared_rank(slot, r);
+    const int cnt = s->ngather;
+    const unsigned long long* src = cluster.map_shared_rank(gath, r);
+    for (int i = threadIdx.x; i < cnt; i += NT) keys[base + i] = src[i];
+    base += cnt;
+  }
+  for (int i = n + threadIdx.x; i < np2; i += NT) keys[i] = 0ull;
+  __syncthreads();
+  bitonic_desc<NT>(keys, np2);
+  const float c1 = rs.c1, nM = rs.nM, Sf = rs.Sf;
+  const int per = (n + NT - 1) / NT;
+  const int i0 = threadIdx.x * per;
+  double local = 0.0;
+  for (int i = i0; i < i0 + per && i < n; ++i)
+    local += double(__fdiv_rn(unnorm(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
+  double incl = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    const double v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  double* wsum = reinterpret_cast<double*>(ms.wF);
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  double run = incl - local;
+  for (int w = 0; w < warp; ++w) run += wsum[w];
+  int kept = 0;
+  for (int i = i0; i < i0 + per && i < n; ++i) {
+    const bool ok = (!rs.p_on || run <= double(rs.tp)) && (!rs.k_on || i < rs.k);
+    if (!ok) break;
+    ++kept;
+    run += double(__fdiv_rn(unnorm(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
+  }
+  const bool complete = kept == max(0, min(per, n - i0));
+  const unsigned bal = __ballot_sync(0xffffffffu, !complete);
+  int* kc = reinterpret_cast<int*>(ms.wcnt);
+  if (lane == 0) kc[warp] = bal ? (warp * 32 + __ffs(bal) - 1) : 0x7FFFFFFF;
+  __syncthreads();
+  int first_incomplete = 0x7FFFFFFF;
+  for (int w = 0; w < NW; ++w) first_incomplete = min(first_incomplete, kc[w]);
+  int* s_nk = ms.slow_int;
+  if (int(threadIdx.x) == first_incomplete) *s_nk = i0 + kept;
+  if (threadIdx.x == 0 && first_incomplete == 0x7FFFFFFF) *s_nk = n;
+  __syncthreads();
+  const int nK = max(1, min(*s_nk, n));
+  const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+  const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
+  NoiseRoot rt{0.f, 0};
+  int64_t gs = -1;
+  int mem_s = 0;
+  if (!a.noise) {
+    rt = noise_root(key, V);
+    token_group(rt.s, V, &gs, &mem_s);
+  }
+  float br = -INFINITY;
+  int bid = 0x7FFFFFFF;
+  for (int i = threadIdx.x; i < nK; i += NT) {
+    const float x = key_to_float(uint32_t(keys[i] >> 32));
+    const int id = int(0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFu));
+    const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
+    const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + id) : tree_noise(key, rt, gs, mem_s, id, V);
+    const float r = __fdiv_rn(pv, E);
+    if (rbetter(r, id, br, bid)) { br = r; bid = id; }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float orr = __shfl_xor_sync(0xffffffffu, br, o);
+    const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+    if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; }
+  }
+  __syncthreads();
+  float* wr = ms.wb;
+  int* wi = ms.wbslot;
+  if (lane == 0) { wr[warp] = br; wi[warp] = bid; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
+    if (bid == 0x7FFFFFFF) bid = int(0xFFFFFFFFu - uint32_t(keys[0] & 0xFFFFFFFFu));
+    a.out_ids[row] = bid;
+    if (a.out_status) a.out_status[row] = QE_ROW_GATHERED;
   }
   __syncthreads();
 }
@@ -492,6 +593,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
   uint32_t* pen = reinterpret_cast<uint32_t*>(smem + SM::pen_off(P.cap));
   unsigned long long* gath = reinterpret_cast<unsigned long long*>(smem + SM::gather_off(P.cap));
   Share* share = reinterpret_cast<Share*>(smem + SM::share_off(P.cap));
+  Share* peers = reinterpret_cast<Share*>(smem + SM::peer_off(P.cap));
   Cand* wl_all = reinterpret_cast<Cand*>(smem + SM::wl_off(P.cap));
   RowState& rs = *reinterpret_cast<RowState*>(smem + SM::rs_off(P.cap));
   Misc& ms = *reinterpret_cast<Misc*>(smem + SM::misc_off(P.cap));
@@ -504,11 +606,13 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
   const int64_t V = a.vocab;
   const Geo geo = make_geo<U>(q, V);
   const int n_cta = int(geo.cta_end - geo.cta_start);
-  int ex = 0;  // exchange counter (alternating share slots)
+  int ex = 0;
 
   if (threadIdx.x == 0) {
     mbar_init(&ms.mbar, 1);
     ms.err = 0;
+    for (int g = 0; g <= kNumSlices; ++g) ms.tstart[g] = slice_start(g, V);
+    for (int g = 0; g < kNumSlices; ++g) ms.tgbase[g] = slice_group_base(g, V);
   }
   __syncthreads();
   uint32_t phase = 0;
@@ -534,30 +638,28 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     const bool small_k = !greedy && k_on && kk <= kSmallK && kk > 1;
     const bool need_race = !greedy && !(k_on && kk == 1) && !small_k;
     const float c1 = greedy ? 0.f : temp_coef(T_);
+    const bool parity = a.noise != nullptr;
 
     // ------------------------------------------------------------ load the CTA's share of the row
     const unsigned char* src_row = static_cast<const unsigned char*>(a.logits) + row * a.ld * int64_t(sizeof(T));
     const size_t nbytes = size_t(n_cta) * sizeof(T);
     const size_t bulk = P.tma_ok ? (nbytes & ~size_t(15)) : 0;
     if (threadIdx.x == 0) {
-      ms.nan = 0; ms.gmin = 0xFFFFFFFFu; ms.umaxkey[0] = ms.umaxkey[1] = 0u;
-      ms.ngather = 0; ms.overflow = 0;
+      ms.nan = 0; ms.gmin = 0xFFFFFFFFu; ms.umaxkey[0] = ms.umaxkey[1] = 0u; ms.ngather = 0;
       if (bulk) {
         fence_proxy_async();
         mbar_expect_tx(&ms.mbar, uint32_t(bulk));
         const unsigned char* src = src_row + geo.cta_start * int64_t(sizeof(T));
         for (size_t o = 0; o < bulk; o += 32768) {
-          const uint32_t n = uint32_t((bulk - o) < 32768 ? (bulk - o) : 32768);
-          bulk_g2s(static_cast<unsigned char*>(data) + o, src + o, n, &ms.mbar);
+          const uint32_t nb = uint32_t((bulk - o) < 32768 ? (bulk - o) : 32768);
+          bulk_g2s(static_cast<unsigned char*>(data) + o, src + o, nb, &ms.mbar);
         }
       }
     }
-    // non-bulk part (unaligned rows or the ragged tail)
     {
       const T* src = reinterpret_cast<const T*>(src_row) + geo.cta_start;
       T* dst = static_cast<T*>(data);
       for (int i = int(bulk / sizeof(T)) + threadIdx.x; i < n_cta; i += NT) dst[i] = src[i];
-      // pad to a multiple of 8 elements (read as -inf by the 8-wide loads)
     }
     if (use_pen) {
       const int nw = n_cta / 32 + 1;
@@ -579,15 +681,28 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     }
     __syncthreads();
 
-    // ------------------------------------------------------------ pass A: group maxima
-    float gmax[kMaxItems][2];
-    float gEmin[kMaxItems][2];
+    // the noise root (one lane of the last warp, overlapping pass 1)
+    if (threadIdx.x == NT - 1 && need_race && !parity) {
+      const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+      const NoiseKey nk = make_noise_key(a.seed, step, a.row_offset + row);
+      const NoiseRoot rt = noise_root(nk, V);
+      int g = 0;
+#pragma unroll
+      for (int st = 8; st >= 1; st >>= 1)
+        if (g + st < kNumSlices && ms.tstart[g + st] <= rt.s) g += st;
+      const int64_t o = rt.s - ms.tstart[g];
+      ms.e_root = rt.e_root;
+      ms.s_gid = ms.tgbase[g] + local_group(o);
+      ms.s_mem = member_index(o);
+    }
+    // ------------------------------------------------------------ pass 1: group max and group-relative sums
+    float gmax[kSlots], fsum[kSlots], gE[kSlots];
     bool lnan = false;
 #pragma unroll
     for (int k = 0; k < kMaxItems; ++k) {
-      gmax[k][0] = gmax[k][1] = -INFINITY;
-      gEmin[k][0] = gEmin[k][1] = INFINITY;
       const int item = warp + k * NW;
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) { gmax[2 * k + tt] = -INFINITY; fsum[2 * k + tt] = 0.f; gE[2 * k + tt] = INFINITY; }
       if (item < geo.nitems) {
         int u, p;
         item_of(geo, item, u, p);
@@ -596,6 +711,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
         for (int tt = 0; tt < 2; ++tt) {
           const int t = 2 * p + tt;
           if (t < un.ntiles) {
+            float m = -INFINITY, em = INFINITY;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
               const int local = t * kTile + b * 256 + lane * 8;
@@ -605,33 +721,45 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
                 float x[8];
                 Load8<T>::run(data, off, nv, x);
                 if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
-                float m = gmax[k][tt];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) { m = fmaxf(m, x[i]); lnan |= (x[i] != x[i]); }
-                gmax[k][tt] = m;
-                if (a.noise && !greedy) {
+                if (parity && need_race) {
                   const float* nz = a.noise + row * a.noise_ld + geo.cta_start + off;
-                  float E[8];
                   if (P.noise_vec && nv >= 8) {
                     const float4 v0 = __ldg(reinterpret_cast<const float4*>(nz));
                     const float4 v1 = __ldg(reinterpret_cast<const float4*>(nz) + 1);
-                    E[0] = v0.x; E[1] = v0.y; E[2] = v0.z; E[3] = v0.w;
-                    E[4] = v1.x; E[5] = v1.y; E[6] = v1.z; E[7] = v1.w;
+                    em = fminf(em, fminf(fminf(fminf(v0.x, v0.y), fminf(v0.z, v0.w)),
+                                         fminf(fminf(v1.x, v1.y), fminf(v1.z, v1.w))));
                   } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) E[i] = i < nv ? __ldg(nz + i) : INFINITY;
+                    for (int i = 0; i < 8; ++i) if (i < nv) em = fminf(em, __ldg(nz + i));
                   }
-                  float e = gEmin[k][tt];
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) e = fminf(e, E[i]);
-                  gEmin[k][tt] = e;
                 }
               }
             }
+            gmax[2 * k + tt] = m;
+            gE[2 * k + tt] = em;
+            if (!greedy && m > -INFINITY && m < INFINITY) {
+              const float c0g = max_coef(m, c1);
+              float fs = 0.f;
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const int local = t * kTile + b * 256 + lane * 8;
+                const int nv = un.L - local;
+                if (nv > 0) {
+                  const int off = un.uoff + local;
+                  float x[8];
+                  Load8<T>::run(data, off, nv, x);
+                  if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) fs = __fadd_rn(fs, unnorm(x[i], c1, c0g));
+                }
+              }
+              fsum[2 * k + tt] = fs;
+            }
           }
         }
-        // unit max: warp reduction, one shared atomic per item
-        const float im = fmaxf(gmax[k][0], gmax[k][1]);
+        const float im = fmaxf(gmax[2 * k], gmax[2 * k + 1]);
         const unsigned int key = __reduce_max_sync(0xffffffffu, ordered_key(isnan(im) ? -INFINITY : im));
         if (lane == 0) atomicMax(&ms.umaxkey[u], key);
       }
@@ -639,10 +767,11 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     if (__any_sync(0xffffffffu, lnan) && lane == 0) ms.nan = 1;
     __syncthreads();
     const bool cnan = ms.nan != 0;
-    float umax[2] = {key_to_float(ms.umaxkey[0]), key_to_float(ms.umaxkey[1])};
-    if (ms.umaxkey[0] == 0u) umax[0] = -INFINITY;
-    if (ms.umaxkey[1] == 0u) umax[1] = -INFINITY;
+    float umax[2] = {ms.umaxkey[0] ? key_to_float(ms.umaxkey[0]) : -INFINITY,
+                     ms.umaxkey[1] ? key_to_float(ms.umaxkey[1]) : -INFINITY};
     const float cmax = fmaxf(umax[0], umax[1]);
+    const float c0 = max_coef(cmax, c1);
+    const bool race_ok = need_race && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY;
 
     // greedy: first id holding the CTA max (NaN first if any)
 #pragma unroll
@@ -654,11 +783,9 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
         const Unit un = unit_of(geo, u);
 #pragma unroll
         for (int tt = 0; tt < 2; ++tt) {
-          const float gm = gmax[k][tt];
-          const bool scan = cnan || (gm == cmax && n_cta > 0);
-          if (scan) {
-            const int t = 2 * p + tt;
-            const int lg = t * 32 + lane;
+          const float gm = gmax[2 * k + tt];
+          if (cnan || (gm == cmax && n_cta > 0)) {
+            const int lg = (2 * p + tt) * 32 + lane;
             for (int m = 0; m < 32; ++m) {
               const int local = int(member_offset(lg, m));
               if (local >= un.L) continue;
@@ -675,74 +802,62 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
 
     // small top-k: per-warp top-8 group maxima -> CTA lower bound of the k-th largest
     if (small_k) {
-      uint32_t keys[kMaxItems * 2];
+      uint32_t keys[kSlots];
 #pragma unroll
-      for (int k = 0; k < kMaxItems; ++k)
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
-          const float gm = gmax[k][tt];
-          keys[k * 2 + tt] = (gm > -INFINITY && !isnan(gm)) ? ordered_key(gm) : 0u;
-        }
+      for (int s = 0; s < kSlots; ++s)
+        keys[s] = (gmax[s] > -INFINITY && !isnan(gmax[s])) ? ordered_key(gmax[s]) : 0u;
       for (int round = 0; round < 8; ++round) {
         uint32_t lb = 0;
 #pragma unroll
-        for (int i = 0; i < kMaxItems * 2; ++i) lb = max(lb, keys[i]);
+        for (int s = 0; s < kSlots; ++s) lb = max(lb, keys[s]);
         const uint32_t m = __reduce_max_sync(0xffffffffu, lb);
         if (lane == 0) ms.wtop[warp * 8 + round] = m;
         const uint32_t who = __ballot_sync(0xffffffffu, lb == m && m != 0u);
-        if (who && lane == ctz_lane(who)) {
+        if (who && lane == __ffs(who) - 1) {
+          bool cleared = false;
 #pragma unroll
-          for (int i = 0; i < kMaxItems * 2; ++i)
-            if (keys[i] == m) { keys[i] = 0u; break; }
+          for (int s = 0; s < kSlots; ++s)
+            if (!cleared && keys[s] == m) { keys[s] = 0u; cleared = true; }
         }
       }
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kMaxR; ++i) wl[i] = Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
     }
     __syncthreads();
     uint32_t topk_lkey = 0u;
     if (small_k && warp == 0) {
-      // k-th largest of the NW*8 warp maxima (bisection on the ordered key)
-      uint32_t v[NW * 8 / 32];
+      constexpr int PER = NW * 8 / 32;
+      uint32_t v[PER];
 #pragma unroll
-      for (int i = 0; i < NW * 8 / 32; ++i) v[i] = ms.wtop[lane + 32 * i];
+      for (int i = 0; i < PER; ++i) v[i] = ms.wtop[lane + 32 * i];
       uint32_t L = 0;
       for (int bit = 31; bit >= 0; --bit) {
         const uint32_t tryk = L | (1u << bit);
         int c = 0;
 #pragma unroll
-        for (int i = 0; i < NW * 8 / 32; ++i) c += __popc(__ballot_sync(0xffffffffu, v[i] >= tryk));
+        for (int i = 0; i < PER; ++i) c += __popc(__ballot_sync(0xffffffffu, v[i] >= tryk));
         if (c >= kk) L = tryk;
       }
       topk_lkey = L;
     }
 
     // ------------------------------------------------------------ race (local, CTA scale)
-    const float c0 = max_coef(cmax, c1);
-    const bool race_ok = need_race && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY;
-    const int Rr = !(p_on || k_on) ? 1 : (p_on && !k_on ? (tp >= 0.9f ? 2 : (tp >= 0.75f ? 3 : 4)) : 4);
-    if (lane == 0) {
-      for (int i = 0; i < kMaxR; ++i) wl[i] = Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
-    }
-    __syncwarp();
-    NoiseKey nkey;
-    NoiseRoot root{0.f, 0};
+    const int Rr = !(p_on || k_on) ? 1 : ((p_on && !k_on && tp >= 0.9f) ? 2 : 4);
+    float bnd[kSlots];
+    uint32_t uw[kSlots], sw[kSlots];
+    unsigned done_mask = 0;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) { bnd[s] = -1.f; uw[s] = 0u; sw[s] = 0u; }
+    float e_root = 0.f;
     int64_t gid_s = -1;
     int mem_s = 0;
+    NoiseKey nkey{0, 0, 0, 0, 0};
     if (race_ok) {
       const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
       nkey = make_noise_key(a.seed, step, a.row_offset + row);
-      if (!a.noise) {
-        root = noise_root(nkey, V);
-        token_group(root.s, V, &gid_s, &mem_s);
-      }
-    }
-    float bound[kMaxItems][2];
-    int garg[kMaxItems][2];
-    bool done_g[kMaxItems][2];
-#pragma unroll
-    for (int k = 0; k < kMaxItems; ++k)
-#pragma unroll
-      for (int tt = 0; tt < 2; ++tt) { bound[k][tt] = -1.f; garg[k][tt] = 0; done_g[k][tt] = false; }
-    if (race_ok) {
+      if (!parity) { e_root = ms.e_root; gid_s = ms.s_gid; mem_s = ms.s_mem; }
 #pragma unroll
       for (int k = 0; k < kMaxItems; ++k) {
         const int item = warp + k * NW;
@@ -750,255 +865,181 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           int u, p;
           item_of(geo, item, u, p);
           const Unit un = unit_of(geo, u);
-          const uint32_t ctr = uint32_t(un.pbase + p * 32 + lane);
           U4 w{0, 0, 0, 0};
-          if (!a.noise) w = philox_at(nkey, ctr, kTagGroup);
+          if (!parity) w = philox_at(nkey, uint32_t(un.pbase + p * 32 + lane), kTagGroup);
 #pragma unroll
           for (int tt = 0; tt < 2; ++tt) {
+            const int s = 2 * k + tt;
             const int t = 2 * p + tt;
             const int lg = t * 32 + lane;
             const int n = t < un.ntiles ? group_size(lg, un.L) : 0;
-            if (n > 0 && gmax[k][tt] > -INFINITY) {
-              float emin;
-              if (a.noise) {
-                emin = gEmin[k][tt];
-              } else {
-                const int64_t gid = un.gbase + lg;
-                if (gid == gid_s) { emin = root.e_root; garg[k][tt] = mem_s; }
-                else {
-                  const GroupMin gmn = tt ? group_min_from(root, w.z, w.w, n) : group_min_from(root, w.x, w.y, n);
-                  emin = gmn.e_min; garg[k][tt] = gmn.arg;
-                }
-              }
-              gEmin[k][tt] = emin;
-              bound[k][tt] = __fdividef(unnorm(gmax[k][tt], c1, c0), emin);
+            uw[s] = tt ? w.z : w.x;
+            sw[s] = tt ? w.w : w.y;
+            if (n > 0 && gmax[s] > -INFINITY) {
+              float ea;
+              if (parity) ea = gE[s];
+              else if (un.gbase + lg == gid_s) ea = e_root;
+              else ea = e_root + (-0.6931472f * __log2f(uniform_open(uw[s]))) * __frcp_rn(float(n));
+              bnd[s] = __fdividef(unnorm(gmax[s], c1, c0), ea);
             }
           }
         }
       }
     }
-    // warp-cooperative evaluation of one group (owner lane ol, item k, tile parity tt)
-    auto eval_group = [&](int k, int tt, int ol) {
+    // warp-cooperative exact evaluation of slot `s` of lane `ol`
+    auto eval_group = [&](int s, int ol) {
+      const int k = s >> 1, tt = s & 1;
       const int item = warp + k * NW;
       int u, p;
       item_of(geo, item, u, p);
       const Unit un = unit_of(geo, u);
       const int t = 2 * p + tt;
       const int lg = t * 32 + ol;
-      float em_own = 0.f;
-      int ag_own = 0;
+      const int n = group_size(lg, un.L);
+      uint32_t uo = 0, so = 0;
+      float eo = 0.f;
 #pragma unroll
-      for (int kq = 0; kq < kMaxItems; ++kq)
-#pragma unroll
-        for (int tq = 0; tq < 2; ++tq)
-          if (kq == k && tq == tt) { em_own = gEmin[kq][tq]; ag_own = garg[kq][tq]; }
-      const float emin = __shfl_sync(0xffffffffu, em_own, ol);
-      const int arg = __shfl_sync(0xffffffffu, ag_own, ol);
+      for (int sq = 0; sq < kSlots; ++sq) if (sq == s) { uo = uw[sq]; so = sw[sq]; eo = gE[sq]; }
+      uo = __shfl_sync(0xffffffffu, uo, ol);
+      so = __shfl_sync(0xffffffffu, so, ol);
+      eo = __shfl_sync(0xffffffffu, eo, ol);
+      float emin = eo;
+      int arg = -1;
+      if (!parity) {
+        if (un.gbase + lg == gid_s) { emin = e_root; arg = mem_s; }
+        else { const GroupMin gm = group_min_from(NoiseRoot{e_root, 0}, uo, so, n); emin = gm.e_min; arg = gm.arg; }
+      }
       const int local = int(member_offset(lg, lane));
       float r = -INFINITY, x = 0.f, E = 1.f;
       int id = 0x7FFFFFFF;
       if (local < un.L) {
         x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
         id = int(geo.cta_start + un.uoff + local);
-        if (a.noise) E = __ldg(a.noise + row * a.noise_ld + id);
-        else E = lane == arg ? emin : __fadd_rn(emin, neglog(uniform_open([&] {
-                   const U4 tw = philox_at(nkey, uint32_t(id >> 2), kTagToken);
-                   const int s = id & 3;
-                   return s == 0 ? tw.x : s == 1 ? tw.y : s == 2 ? tw.z : tw.w;
-                 }())));
+        if (parity) {
+          E = __ldg(a.noise + row * a.noise_ld + id);
+        } else if (lane == arg) {
+          E = emin;
+        } else {
+          const U4 tw = philox_at(nkey, uint32_t(id >> 2), kTagToken);
+          const int sel = id & 3;
+          const uint32_t word = sel == 0 ? tw.x : sel == 1 ? tw.y : sel == 2 ? tw.z : tw.w;
+          E = __fadd_rn(emin, neglog(uniform_open(word)));
+        }
         r = __fdiv_rn(unnorm(x, c1, c0), E);
         if (r != r) r = -INFINITY;
       }
       warp_merge(wl, Rr, r, x, E, id);
     };
     if (race_ok) {
-      // R1: each warp expands its best-bound group
-      float bb = -1.f; int bk = 0, btt = 0;
+      // seed: the CTA's best-bound group, expanded by its warp
+      float bb = -1.f;
+      int bs = 0;
 #pragma unroll
-      for (int k = 0; k < kMaxItems; ++k)
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt)
-          if (bound[k][tt] > bb) { bb = bound[k][tt]; bk = k; btt = tt; }
-      float wb = bb; int wlane = lane;
+      for (int s = 0; s < kSlots; ++s) if (bnd[s] > bb) { bb = bnd[s]; bs = s; }
+      int code = lane * 8 + bs;
       for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, wb, o);
-        const int ol = __shfl_xor_sync(0xffffffffu, wlane, o);
-        if (ob > wb || (ob == wb && ol < wlane)) { wb = ob; wlane = ol; }
+        const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
+        const int oc = __shfl_xor_sync(0xffffffffu, code, o);
+        if (ob > bb || (ob == bb && oc < code)) { bb = ob; code = oc; }
       }
-      if (wb > 0.f) {
-        const int k = __shfl_sync(0xffffffffu, bk, wlane), tt = __shfl_sync(0xffffffffu, btt, wlane);
-        if (lane == wlane) {
-#pragma unroll
-          for (int kq = 0; kq < kMaxItems; ++kq)
-#pragma unroll
-            for (int tq = 0; tq < 2; ++tq)
-              if (kq == k && tq == tt) done_g[kq][tq] = true;
-        }
-        eval_group(k, tt, wlane);
-      }
+      if (lane == 0) { ms.wb[warp] = bb; ms.wbslot[warp] = code; }
     }
     __syncthreads();
-    if (race_ok && warp == 0) {
-      // CTA threshold: the Rr-th best ratio over all warp lists
-      float v[NW * kMaxR / 32 > 0 ? (NW * kMaxR + 31) / 32 : 1];
-      constexpr int PER = (NW * kMaxR + 31) / 32;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int idx = lane + 32 * i;
-        v[i] = (idx < NW * kMaxR && (idx % kMaxR) < Rr) ? wl_all[idx].r : -INFINITY;
-      }
-      float th = -INFINITY;
-      for (int round = 0; round < Rr; ++round) {
-        float m = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) m = fmaxf(m, v[i]);
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        th = m;
-        const uint32_t who = __ballot_sync(0xffffffffu, [&] {
-          bool h = false;
-#pragma unroll
-          for (int i = 0; i < PER; ++i) h |= (v[i] == m);
-          return h;
-        }());
-        if (who && lane == ctz_lane(who)) {
-#pragma unroll
-          for (int i = 0; i < PER; ++i) if (v[i] == m) { v[i] = -INFINITY; break; }
-        }
-      }
-      if (lane == 0) ms.theta = th > -INFINITY ? th : 0.f;
-    }
-    __syncthreads();
+    int bw = 0;
     if (race_ok) {
-      // R2: expand every group whose bound can still reach the threshold
-      float theta = ms.theta;
-      for (;;) {
-        bool any = false;
-        int fk = 0, ftt = 0;
-#pragma unroll
-        for (int k = 0; k < kMaxItems; ++k)
-#pragma unroll
-          for (int tt = 0; tt < 2; ++tt)
-            if (!any && !done_g[k][tt] && bound[k][tt] > 0.f && bound[k][tt] >= theta * 0.99998f) {
-              any = true; fk = k; ftt = tt;
-            }
-        const uint32_t who = __ballot_sync(0xffffffffu, any);
-        if (!who) break;
-        const int ol = ctz_lane(who);
-        const int k = __shfl_sync(0xffffffffu, fk, ol), tt = __shfl_sync(0xffffffffu, ftt, ol);
-        if (lane == ol) {
-#pragma unroll
-          for (int kq = 0; kq < kMaxItems; ++kq)
-#pragma unroll
-            for (int tq = 0; tq < 2; ++tq)
-              if (kq == k && tq == tt) done_g[kq][tq] = true;
-        }
-        eval_group(k, tt, ol);
-        __syncwarp();
-        theta = fmaxf(theta, wl[Rr - 1].r);
+      for (int w = 1; w < NW; ++w) if (ms.wb[w] > ms.wb[bw]) bw = w;
+      if (ms.wb[bw] > 0.f && warp == bw) {
+        const int code = ms.wbslot[bw];
+        if (lane == (code >> 3)) done_mask |= 1u << (code & 7);
+        eval_group(code & 7, code >> 3);
       }
     }
     __syncthreads();
 
-    // ------------------------------------------------------------ exchange 1
-    Share& my = share[ex & 1];
-    if (warp == 0) {
-      // CTA top-Rr from the warp lists
-      constexpr int PER = (NW * kMaxR + 31) / 32;
-      Cand c[PER];
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int idx = lane + 32 * i;
-        c[i] = (race_ok && idx < NW * kMaxR && (idx % kMaxR) < Rr) ? wl_all[idx] : Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
-      }
-      int n = 0;
-      for (int round = 0; round < Rr; ++round) {
-        int bi = 0;
-#pragma unroll
-        for (int i = 1; i < PER; ++i) if (rbetter(c[i].r, c[i].id, c[bi].r, c[bi].id)) bi = i;
-        float br = c[bi].r; int bid = c[bi].id; int bl = lane;
-        for (int o = 16; o; o >>= 1) {
-          const float orr = __shfl_xor_sync(0xffffffffu, br, o);
-          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-          const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
-          if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; bl = ol; }
-        }
-        if (!(br > -INFINITY)) break;
-        if (lane == bl) { my.cand[n] = c[bi]; c[bi].r = -INFINITY; c[bi].id = 0x7FFFFFFF; }
-        ++n;
-      }
-      if (lane == 0) {
-        my.ncand = n;
+    // ------------------------------------------------------------ exchange 1: maxima, greedy, race seeds
+    {
+      Share& my = share[ex & 1];
+      if (threadIdx.x == 0) {
         my.umax[0] = umax[0]; my.umax[1] = umax[1];
         my.cmax = cnan ? NAN : cmax;
         my.c0 = c0;
         my.nan = cnan ? 1 : 0;
         my.gidx = int(ms.gmin == 0xFFFFFFFFu ? 0x7FFFFFFF : ms.gmin);
         my.gval = cnan ? NAN : cmax;
-        my.topk_lkey = topk_lkey;
-      }
-    }
-    cluster.sync();
-    if (threadIdx.x == 0) {
-      // every CTA computes the same row state from the same shares
-      float xM = -INFINITY; bool nan = false; float gv = -INFINITY; int gi = 0x7FFFFFFF;
-      uint32_t lkey = 0u;
-      for (int r = 0; r < CL; ++r) {
-        const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
-        nan |= s->nan != 0;
-        if (s->gidx != 0x7FFFFFFF && argmax_better(s->gval, s->gidx, gv, gi)) { gv = s->gval; gi = s->gidx; }
-        for (int u = 0; u < U; ++u) {
-          rs.umax[r * U + u] = s->umax[u];
-          xM = fmaxf(xM, s->umax[u]);
-        }
-        lkey = max(lkey, s->topk_lkey);
-      }
-      const float nM = max_coef(xM, c1);
-      rs.xM = xM; rs.nM = nM; rs.c1 = c1;
-      rs.p_on = p_on; rs.k_on = k_on; rs.k = kk; rs.tp = tp;
-      rs.L = lkey ? key_to_float(lkey) : -INFINITY;
-      const bool nonfinite = nan || !(xM > -INFINITY) || xM == INFINITY || (!greedy && !(fabsf(nM) < INFINITY));
-      rs.status = greedy ? QE_ROW_GREEDY : (nonfinite ? QE_ROW_NONFINITE : 0);
-      rs.out = gi == 0x7FFFFFFF ? 0 : gi;
-      if (greedy || nonfinite || (k_on && kk == 1)) {
-        rs.type = kDone;
-      } else if (small_k) {
-        rs.type = kGather;
-      } else {
-        // merge the CTA candidate lists (scaled to the row max)
+        my.lkey = topk_lkey;
         int n = 0;
-        Cand best[kMaxR];
-        double bestr[kMaxR];
-        for (int r = 0; r < CL; ++r) {
-          const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
-          const double sc = exp2(double(nM) - double(s->c0));
-          for (int i = 0; i < s->ncand; ++i) {
-            Cand c = s->cand[i];
-            const double rv = double(c.r) * sc;
-            int j = n < Rr ? n : Rr - 1;
-            if (n >= Rr && !(rv > bestr[Rr - 1] || (rv == bestr[Rr - 1] && c.id < best[Rr - 1].id))) continue;
-            while (j > 0 && (rv > bestr[j - 1] || (rv == bestr[j - 1] && c.id < best[j - 1].id))) {
-              best[j] = best[j - 1]; bestr[j] = bestr[j - 1]; --j;
-            }
-            best[j] = c; bestr[j] = rv;
-            if (n < Rr) ++n;
+        if (race_ok)
+          for (int i = 0; i < Rr; ++i) if (wl_all[bw * kMaxR + i].r > -INFINITY) my.cand[n++] = wl_all[bw * kMaxR + i];
+        my.ncand = n;
+      }
+      cluster.sync();
+      if (warp == 0) {
+        // lane r reads peer r
+        float pm = -INFINITY, pc0 = 0.f, gv = -INFINITY;
+        int pn = 0, gi = 0x7FFFFFFF, pnc = 0;
+        uint32_t lk = 0u;
+        float sr[kMaxR];
+#pragma unroll
+        for (int i = 0; i < kMaxR; ++i) sr[i] = -INFINITY;
+        if (lane < CL) {
+          const Share* sp = cluster.map_shared_rank(&share[ex & 1], lane);
+          for (int u = 0; u < U; ++u) pm = fmaxf(pm, sp->umax[u]);
+          pc0 = sp->c0; pn = sp->nan; gi = sp->gidx; gv = sp->gval; lk = sp->lkey; pnc = sp->ncand;
+#pragma unroll
+          for (int i = 0; i < kMaxR; ++i) if (i < pnc) sr[i] = sp->cand[i].r;
+          ms.c0peer[lane] = pc0;
+        }
+        const bool anynan = __any_sync(0xffffffffu, pn != 0);
+        float xM = pm;
+        for (int o = 16; o; o >>= 1) xM = fmaxf(xM, __shfl_xor_sync(0xffffffffu, xM, o));
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
+          if (oi != 0x7FFFFFFF && (gi == 0x7FFFFFFF || argmax_better(ov, oi, gv, gi))) { gv = ov; gi = oi; }
+        }
+        lk = __reduce_max_sync(0xffffffffu, lk);
+        const float nM = max_coef(xM, c1);
+        // global race threshold: the Rr-th best seed ratio, in row scale
+        const float sc = lane < CL ? exp2f(nM - pc0) : 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxR; ++i) sr[i] = sr[i] > -INFINITY ? sr[i] * sc : -INFINITY;
+        float th = 0.f;
+        for (int round = 0; round < Rr; ++round) {
+          float m = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < kMaxR; ++i) m = fmaxf(m, sr[i]);
+          for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (!(m > -INFINITY)) { th = 0.f; break; }
+          th = m;
+          const uint32_t who = __ballot_sync(0xffffffffu, [&] {
+            bool h = false;
+#pragma unroll
+            for (int i = 0; i < kMaxR; ++i) h |= (sr[i] == m);
+            return h;
+          }());
+          if (lane == __ffs(who) - 1) {
+            bool cl = false;
+#pragma unroll
+            for (int i = 0; i < kMaxR; ++i) if (!cl && sr[i] == m) { sr[i] = -INFINITY; cl = true; }
           }
         }
-        for (int i = 0; i < n; ++i) rs.cand[i] = best[i];
-        rs.R = n;
-        if (n == 0) {
-          rs.type = kDone;  // nothing finite to race: keep the greedy choice
-          rs.status = QE_ROW_NONFINITE;
-        } else if (!p_on && !k_on) {
-          rs.type = kDone;
-          rs.out = best[0].id;
-        } else {
-          rs.type = kRaceTest;
+        if (lane == 0) {
+          rs.xM = xM; rs.nM = nM; rs.c1 = c1;
+          rs.p_on = p_on; rs.k_on = k_on; rs.k = kk; rs.tp = tp;
+          rs.L = lk ? key_to_float(lk) : -INFINITY;
+          const bool nonfinite = anynan || !(xM > -INFINITY) || xM == INFINITY || (!greedy && !(fabsf(nM) < INFINITY));
+          rs.status = greedy ? QE_ROW_GREEDY : (nonfinite ? QE_ROW_NONFINITE : 0);
+          rs.out = gi == 0x7FFFFFFF ? 0 : gi;
+          rs.R = 0;
+          rs.theta = th;
+          if (greedy || nonfinite || (k_on && kk == 1)) rs.type = kDone;
+          else if (small_k) rs.type = kGather;
+          else rs.type = kRaceTest;
         }
       }
+      ++ex;
+      __syncthreads();
     }
-    ++ex;
-    __syncthreads();
-
     if (rs.type == kDone) {
       if (q == 0 && threadIdx.x == 0) {
         a.out_ids[row] = rs.out;
@@ -1008,194 +1049,156 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
       continue;
     }
 
-    // ------------------------------------------------------------ pass B
+    if (rs.type == kRaceTest) {
+      // expand every group whose bound can still reach the row threshold
+      // (bounds use approximate logs and divisions: 1e-3 margin)
+      float theta = rs.theta * exp2f(c0 - rs.nM);
+      if (race_ok) {
+        theta = fmaxf(theta, wl[Rr - 1].r);
+        for (;;) {
+          int fs = -1;
+#pragma unroll
+          for (int s = 0; s < kSlots; ++s)
+            if (fs < 0 && !((done_mask >> s) & 1u) && bnd[s] > 0.f && bnd[s] >= theta * 0.999f) fs = s;
+          const uint32_t who = __ballot_sync(0xffffffffu, fs >= 0);
+          if (!who) break;
+          const int ol = __ffs(who) - 1;
+          const int s = __shfl_sync(0xffffffffu, fs, ol);
+          if (lane == ol) done_mask |= 1u << s;
+          eval_group(s, ol);
+          __syncwarp();
+          theta = fmaxf(theta, wl[Rr - 1].r);
+        }
+      }
+      __syncthreads();
+      // ---------------------------------------------------------- exchange 2: candidates
+      Share& my = share[ex & 1];
+      if (warp == 0) {
+        constexpr int PER = (NW * kMaxR + 31) / 32;
+        Cand c[PER];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int idx = lane + 32 * i;
+          c[i] = (race_ok && idx < NW * kMaxR) ? wl_all[idx] : Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
+        }
+        int n = 0;
+        for (int round = 0; round < Rr; ++round) {
+          int bi = 0;
+#pragma unroll
+          for (int i = 1; i < PER; ++i) if (rbetter(c[i].r, c[i].id, c[bi].r, c[bi].id)) bi = i;
+          Cand cb = c[0];
+#pragma unroll
+          for (int i = 1; i < PER; ++i) if (i == bi) cb = c[i];
+          float br = cb.r; int bid = cb.id; int bl = lane;
+          for (int o = 16; o; o >>= 1) {
+            const float orr = __shfl_xor_sync(0xffffffffu, br, o);
+            const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; bl = ol; }
+          }
+          if (!(br > -INFINITY)) break;
+          if (lane == bl) {
+            my.cand[n] = cb;
+#pragma unroll
+            for (int i = 0; i < PER; ++i) if (i == bi) { c[i].r = -INFINITY; c[i].id = 0x7FFFFFFF; }
+          }
+          ++n;
+        }
+        if (lane == 0) my.ncand = n;
+      }
+      cluster.sync();
+      if (warp == 0) {
+        // lane r holds peer r's candidates scaled to the row (double)
+        Cand pc[kMaxR];
+        double pr[kMaxR];
+        int pnc = 0;
+        if (lane < CL) {
+          const Share* sp = cluster.map_shared_rank(&share[ex & 1], lane);
+          pnc = sp->ncand;
+          const double scl = exp2(double(rs.nM) - double(ms.c0peer[lane]));
+#pragma unroll
+          for (int i = 0; i < kMaxR; ++i) {
+            if (i < pnc) { pc[i] = sp->cand[i]; pr[i] = double(pc[i].r) * scl; } else { pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < kMaxR; ++i) { pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
+        }
+        int n = 0;
+        for (int round = 0; round < Rr; ++round) {
+          int bi = 0;
+#pragma unroll
+          for (int i = 1; i < kMaxR; ++i)
+            if (pr[i] > pr[bi] || (pr[i] == pr[bi] && pc[i].id < pc[bi].id)) bi = i;
+          double bv = -1.0; int bid = 0x7FFFFFFF;
+#pragma unroll
+          for (int i = 0; i < kMaxR; ++i) if (i == bi) { bv = pr[i]; bid = pc[i].id; }
+          int bl = lane;
+          for (int o = 16; o; o >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if (ov > bv || (ov == bv && (oid < bid || (oid == bid && ol < bl)))) { bv = ov; bid = oid; bl = ol; }
+          }
+          if (!(bv >= 0.0) || bid == 0x7FFFFFFF) break;
+          if (lane == bl) {
+#pragma unroll
+            for (int i = 0; i < kMaxR; ++i) if (i == bi) { rs.cand[n] = pc[i]; pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
+          }
+          ++n;
+        }
+        if (lane == 0) {
+          rs.R = n;
+          if (n == 0) {
+            rs.type = kDone;
+            rs.status = QE_ROW_NONFINITE;
+          } else if (!p_on && !k_on) {
+            rs.type = kDone;
+          }
+        }
+      }
+      ++ex;
+      __syncthreads();
+      if (rs.type == kDone) {
+        if (q == 0 && threadIdx.x == 0) {
+          a.out_ids[row] = rs.R > 0 ? rs.cand[0].id : rs.out;
+          if (a.out_status) a.out_status[row] = rs.status;
+        }
+        __syncthreads();
+        continue;
+      }
+    }
+
+    // ------------------------------------------------------------ S partial and pass 2 (sparse)
     const float nM = rs.nM;
     const int R = rs.type == kRaceTest ? rs.R : 0;
-    const float Lg = rs.L;
-    float cv[kMaxR];
-    int cid_[kMaxR];
+    unsigned long long sfl = 0ull;
 #pragma unroll
-    for (int c = 0; c < kMaxR; ++c) { cv[c] = c < R ? rs.cand[c].x : 0.f; cid_[c] = c < R ? rs.cand[c].id : 0; }
+    for (int s = 0; s < kSlots; ++s) {
+      if (fsum[s] > 0.f) {
+        const float sc = qe_ex2(__fsub_rn(nM, max_coef(gmax[s], c1)));
+        sfl += __double2ull_rn(double(__fmul_rn(fsum[s], sc)) * kSumScale);
+      }
+    }
+    float cv[kMaxR];
+    int cidv[kMaxR];
+#pragma unroll
+    for (int c = 0; c < kMaxR; ++c) { cv[c] = c < R ? rs.cand[c].x : INFINITY; cidv[c] = c < R ? rs.cand[c].id : 0; }
     float Fl[kMaxR];
     long long Cl[kMaxR];
 #pragma unroll
     for (int c = 0; c < kMaxR; ++c) { Fl[c] = 0.f; Cl[c] = 0; }
-    unsigned long long sfx[2] = {0ull, 0ull};
     const bool gather_row = rs.type == kGather;
-#pragma unroll
-    for (int k = 0; k < kMaxItems; ++k) {
-      const int item = warp + k * NW;
-      if (item < geo.nitems) {
-        int u, p;
-        item_of(geo, item, u, p);
-        const Unit un = unit_of(geo, u);
-        const float um = u ? umax[1] : umax[0];
-        const float c0u = max_coef(um, c1);
-        const bool uok = um > -INFINITY;
-        const float scale = uok ? exp2f(nM - c0u) : 0.f;
-        // candidate thresholds for this unit: x > th (GE via the float below v)
-        float th[kMaxR];
-        bool mixed[kMaxR];
-#pragma unroll
-        for (int c = 0; c < kMaxR; ++c) {
-          mixed[c] = c < R && cid_[c] >= un.ustart && cid_[c] < un.uend;
-          th[c] = (c < R && cid_[c] >= un.uend) ? nextafterf(cv[c], -INFINITY) : cv[c];
-        }
-        float Fi[kMaxR];
-        long long Ci[kMaxR];
-#pragma unroll
-        for (int c = 0; c < kMaxR; ++c) { Fi[c] = 0.f; Ci[c] = 0; }
-        unsigned long long sfu = 0ull;
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
-          const int t = 2 * p + tt;
-          float fs = 0.f;
-          if (t < un.ntiles && uok) {
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const int local = t * kTile + b * 256 + lane * 8;
-              const int nv = max(0, min(8, un.L - local));
-              const int off = un.uoff + local;
-              float x[8];
-              Load8<T>::run(data, off, nv, x);
-              if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float e = unnorm(x[i], c1, c0u);
-                fs = __fadd_rn(fs, e);
-#pragma unroll
-                for (int c = 0; c < kMaxR; ++c) {
-                  if (c < R) {
-                    bool pred = x[i] > th[c];
-                    if (mixed[c]) pred = pred || (x[i] == cv[c] && int(geo.cta_start + off + i) < cid_[c]);
-                    if (pred) { Fi[c] += e; Ci[c] += 1; }
-                  }
-                }
-              }
-              if (gather_row) {
-                unsigned mask = 0;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) mask |= ((i < nv && x[i] >= Lg) ? 1u : 0u) << i;
-                gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
-              }
-            }
-          }
-          if (fs > 0.f) sfu += __double2ull_rn(double(fs) * kSumScale);
-        }
-        if (u) sfx[1] += sfu; else sfx[0] += sfu;
-#pragma unroll
-        for (int c = 0; c < kMaxR; ++c) { Fl[c] += Fi[c] * scale; Cl[c] += Ci[c]; }
+    float Lg = rs.L;
+    // two rounds at most: the candidate tests, then (if every candidate was
+    // rejected) a gather of the tokens >= the best rejected candidate
+    for (int round = 0; round < 2; ++round) {
+      const bool do_gather = round == 1 || gather_row;
+      if (round == 1) {
+        if (threadIdx.x == 0) ms.ngather = 0;
+        __syncthreads();
+        Lg = rs.L;
       }
-    }
-    // reductions: warp -> shared -> thread 0
-#pragma unroll
-    for (int c = 0; c < kMaxR; ++c) {
-      if (c < R) {
-        float f = Fl[c];
-        long long n = Cl[c];
-        for (int o = 16; o; o >>= 1) {
-          f += __shfl_xor_sync(0xffffffffu, f, o);
-          n += __shfl_xor_sync(0xffffffffu, n, o);
-        }
-        if (lane == 0) { ms.wF[warp][c] = f; ms.wcnt[warp][c] = n; }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      unsigned long long s = sfx[u];
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) ms.wsfix[warp][u] = s;
-    }
-    __syncthreads();
-    Share& my2 = share[ex & 1];
-    if (threadIdx.x == 0) {
-      for (int u = 0; u < 2; ++u) {
-        unsigned long long s = 0;
-        for (int w = 0; w < NW; ++w) s += ms.wsfix[w][u];
-        my2.sfix[u] = s;
-      }
-      for (int c = 0; c < R; ++c) {
-        double f = 0.0; long long n = 0;
-        for (int w = 0; w < NW; ++w) { f += double(ms.wF[w][c]); n += ms.wcnt[w][c]; }
-        my2.F[c] = f; my2.cnt[c] = n;
-      }
-      my2.ngather = ms.ngather;
-      my2.overflow = ms.ngather > kGatherCap ? 1 : 0;
-    }
-    cluster.sync();
-    if (threadIdx.x == 0) {
-      double Sd = 0.0;
-      double F[kMaxR];
-      long long C[kMaxR];
-      for (int c = 0; c < kMaxR; ++c) { F[c] = 0.0; C[c] = 0; }
-      int ngat = 0, ovf = 0;
-      for (int r = 0; r < CL; ++r) {
-        const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
-        for (int u = 0; u < U; ++u) {
-          const float um = rs.umax[r * U + u];
-          if (um > -INFINITY) Sd += double(s->sfix[u]) * (1.0 / kSumScale) * exp2(double(nM) - double(max_coef(um, c1)));
-        }
-        for (int c = 0; c < R; ++c) { F[c] += s->F[c]; C[c] += s->cnt[c]; }
-        ngat += s->ngather;
-        ovf |= s->overflow;
-      }
-      rs.S = Sd;
-      rs.Sf = float(Sd);
-      if (!(rs.Sf > 0.f) || rs.Sf == INFINITY) {
-        rs.type = kDone;
-        rs.status = QE_ROW_NONFINITE;
-      } else if (rs.type == kRaceTest) {
-        // exact ratios, then the first candidate inside the kept set
-        int order[kMaxR];
-        for (int c = 0; c < R; ++c) {
-          const float p = __fdiv_rn(unnorm(rs.cand[c].x, c1, nM), rs.Sf);
-          rs.rM[c] = __fdiv_rn(p, rs.cand[c].E);
-          order[c] = c;
-        }
-        for (int i = 1; i < R; ++i) {
-          const int v = order[i];
-          int j = i;
-          while (j > 0 && rbetter(rs.rM[v], rs.cand[v].id, rs.rM[order[j - 1]], rs.cand[order[j - 1]].id)) {
-            order[j] = order[j - 1]; --j;
-          }
-          order[j] = v;
-        }
-        int win = -1;
-        float Lx = -INFINITY;
-        for (int i = 0; i < R; ++i) {
-          const int c = order[i];
-          const bool okp = !p_on || F[c] <= double(tp) * Sd;
-          const bool okk = !k_on || C[c] < kk;
-          if (okp && okk) { win = c; break; }
-          Lx = fmaxf(Lx, rs.cand[c].x);
-        }
-        if (win >= 0) {
-          rs.type = kDone;
-          rs.out = rs.cand[win].id;
-        } else {
-          rs.type = kGather;  // every kept token is >= the best rejected candidate
-          rs.L = Lx;
-        }
-      } else {
-        if (ovf || ngat > P.merge_cap) rs.type = kSlow;
-      }
-      rs.R = ngat;
-    }
-    ++ex;
-    __syncthreads();
-    if (rs.type == kDone) {
-      if (q == 0 && threadIdx.x == 0) {
-        a.out_ids[row] = rs.out;
-        if (a.out_status) a.out_status[row] = rs.status;
-      }
-      __syncthreads();
-      continue;
-    }
-    if (rs.type == kGather && R > 0) {
-      // pass C: gather the keys of every token >= L (no exponentials)
-      if (threadIdx.x == 0) ms.ngather = 0;
-      __syncthreads();
-      const float Lc = rs.L;
 #pragma unroll
       for (int k = 0; k < kMaxItems; ++k) {
         const int item = warp + k * NW;
@@ -1203,10 +1206,25 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           int u, p;
           item_of(geo, item, u, p);
           const Unit un = unit_of(geo, u);
+          // thresholds: a token is ahead of candidate c iff x > th[c]
+          // (>= v for ids below c's, > v above it; c's own slice is mixed)
+          float th[kMaxR];
+          bool mixed[kMaxR];
+#pragma unroll
+          for (int c = 0; c < kMaxR; ++c) {
+            mixed[c] = c < R && cidv[c] >= un.ustart && cidv[c] < un.uend;
+            th[c] = (c < R && cidv[c] >= un.uend) ? nextafterf(cv[c], -INFINITY) : cv[c];
+          }
+          float thmin = INFINITY;
+#pragma unroll
+          for (int c = 0; c < kMaxR; ++c) if (c < R) thmin = fminf(thmin, mixed[c] ? nextafterf(cv[c], -INFINITY) : th[c]);
 #pragma unroll
           for (int tt = 0; tt < 2; ++tt) {
+            const int s = 2 * k + tt;
             const int t = 2 * p + tt;
-            if (t < un.ntiles) {
+            const bool q_test = !do_gather && t < un.ntiles && gmax[s] > thmin;
+            const bool q_gath = do_gather && t < un.ntiles && gmax[s] >= Lg;
+            if (__any_sync(0xffffffffu, q_test || q_gath)) {
 #pragma unroll
               for (int b = 0; b < 4; ++b) {
                 const int local = t * kTile + b * 256 + lane * 8;
@@ -1215,145 +1233,155 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
                 float x[8];
                 Load8<T>::run(data, off, nv, x);
                 if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
-                unsigned mask = 0;
+                if (q_test) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mask |= ((i < nv && x[i] >= Lc) ? 1u : 0u) << i;
-                gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
+                  for (int i = 0; i < 8; ++i) {
+                    if (x[i] > thmin) {
+                      const float e = unnorm(x[i], c1, nM);
+#pragma unroll
+                      for (int c = 0; c < kMaxR; ++c) {
+                        if (c < R) {
+                          bool pred = x[i] > th[c];
+                          if (mixed[c]) pred = pred || (x[i] == cv[c] && int(geo.cta_start + off + i) < cidv[c]);
+                          if (pred) { Fl[c] += e; Cl[c] += 1; }
+                        }
+                      }
+                    }
+                  }
+                }
+                if (do_gather) {
+                  unsigned mask = 0;
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) mask |= ((q_gath && i < nv && x[i] >= Lg) ? 1u : 0u) << i;
+                  gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
+                }
               }
             }
           }
         }
       }
+      // reductions and exchange
+#pragma unroll
+      for (int c = 0; c < kMaxR; ++c) {
+        if (c < R && round == 0) {
+          float f = Fl[c];
+          long long n = Cl[c];
+          for (int o = 16; o; o >>= 1) {
+            f += __shfl_xor_sync(0xffffffffu, f, o);
+            n += __shfl_xor_sync(0xffffffffu, n, o);
+          }
+          if (lane == 0) { ms.wF[warp][c] = f; ms.wcnt[warp][c] = n; }
+        }
+      }
+      if (round == 0) {
+        unsigned long long sv = sfl;
+        for (int o = 16; o; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+        if (lane == 0) ms.wsfix[warp] = sv;
+      }
       __syncthreads();
-      Share& my3 = share[ex & 1];
+      Share& my2 = share[ex & 1];
       if (threadIdx.x == 0) {
-        my3.ngather = ms.ngather;
-        my3.overflow = ms.ngather > kGatherCap ? 1 : 0;
+        if (round == 0) {
+          unsigned long long sv = 0;
+          for (int w = 0; w < NW; ++w) sv += ms.wsfix[w];
+          my2.sfix = sv;
+          for (int c = 0; c < R; ++c) {
+            double f = 0.0; long long n = 0;
+            for (int w = 0; w < NW; ++w) { f += double(ms.wF[w][c]); n += ms.wcnt[w][c]; }
+            my2.F[c] = f; my2.cnt[c] = n;
+          }
+        }
+        my2.ngather = ms.ngather;
+        my2.overflow = ms.ngather > kGatherCap ? 1 : 0;
       }
       cluster.sync();
+      if (threadIdx.x < CL) {
+        const Share* s = cluster.map_shared_rank(&share[ex & 1], int(threadIdx.x));
+        Share& d = peers[threadIdx.x];
+        d.ngather = s->ngather;
+        d.overflow = s->overflow;
+        if (round == 0) {
+          d.sfix = s->sfix;
+          for (int c = 0; c < R; ++c) { d.F[c] = s->F[c]; d.cnt[c] = s->cnt[c]; }
+        }
+      }
+      __syncthreads();
       if (threadIdx.x == 0) {
         int ngat = 0, ovf = 0;
-        for (int r = 0; r < CL; ++r) {
-          const Share* s = cluster.map_shared_rank(&share[ex & 1], r);
-          ngat += s->ngather;
-          ovf |= s->overflow;
+        for (int r = 0; r < CL; ++r) { ngat += peers[r].ngather; ovf |= peers[r].overflow; }
+        if (round == 0) {
+          unsigned long long sv = 0;
+          double F[kMaxR];
+          long long C[kMaxR];
+          for (int c = 0; c < kMaxR; ++c) { F[c] = 0.0; C[c] = 0; }
+          for (int r = 0; r < CL; ++r) {
+            sv += peers[r].sfix;
+            for (int c = 0; c < R; ++c) { F[c] += peers[r].F[c]; C[c] += peers[r].cnt[c]; }
+          }
+          const double Sd = double(sv) * (1.0 / kSumScale);
+          rs.S = Sd;
+          rs.Sf = float(Sd);
+          if (!(rs.Sf > 0.f) || rs.Sf == INFINITY) {
+            rs.type = kDone;
+            rs.status = QE_ROW_NONFINITE;
+          } else if (rs.type == kRaceTest) {
+            // exact ratios; the first candidate in race order inside the kept set wins
+            float rM[kMaxR];
+            int order[kMaxR];
+            for (int c = 0; c < R; ++c) {
+              rM[c] = __fdiv_rn(__fdiv_rn(unnorm(rs.cand[c].x, c1, nM), rs.Sf), rs.cand[c].E);
+              order[c] = c;
+            }
+            for (int i = 1; i < R; ++i) {
+              const int v = order[i];
+              int j = i;
+              while (j > 0 && rbetter(rM[v], rs.cand[v].id, rM[order[j - 1]], rs.cand[order[j - 1]].id)) {
+                order[j] = order[j - 1]; --j;
+              }
+              order[j] = v;
+            }
+            int win = -1;
+            float Lx = -INFINITY;
+            for (int i = 0; i < R; ++i) {
+              const int c = order[i];
+              const bool okp = !p_on || F[c] <= double(tp) * Sd;
+              const bool okk = !k_on || C[c] < kk;
+              if (okp && okk) { win = c; break; }
+              Lx = fmaxf(Lx, rs.cand[c].x);
+            }
+            if (win >= 0) {
+              rs.type = kDone;
+              rs.out = rs.cand[win].id;
+            } else {
+              rs.type = kGather;  // every kept token is >= the best rejected candidate
+              rs.L = Lx;
+            }
+          } else if (ovf || ngat > P.merge_cap) {
+            rs.type = kSlow;
+          }
+        } else if (ovf || ngat > P.merge_cap) {
+          rs.type = kSlow;
         }
-        rs.R = ngat;
-        if (ovf || ngat > P.merge_cap) rs.type = kSlow;
+        rs.R = rs.type == kGather ? ngat : rs.R;
+        if (round == 0 && rs.type == kGather && !gather_row) rs.R = -1;  // needs the gather round
       }
       ++ex;
       __syncthreads();
+      if (!(rs.type == kGather && rs.R == -1)) break;
     }
-
-    if (rs.type == kGather) {
-      // CTA 0 finishes the row exactly from the gathered keys; the others move on
-      if (q == 0) {
-        unsigned long long* keys = reinterpret_cast<unsigned long long*>(data);
-        const int n = rs.R;
-        int np2 = 1;
-        while (np2 < n) np2 <<= 1;
-        // copy every CTA's list (their lists stay intact until CTA 0 joins the next exchange)
-        int base = 0;
-        for (int r = 0; r < CL; ++r) {
-          const Share* s = cluster.map_shared_rank(&share[(ex - 1) & 1], r);
-          const int cnt = s->ngather;
-          const unsigned long long* src = cluster.map_shared_rank(gath, r);
-          for (int i = threadIdx.x; i < cnt; i += NT) keys[base + i] = src[i];
-          base += cnt;
-        }
-        for (int i = n + threadIdx.x; i < np2; i += NT) keys[i] = 0ull;
-        __syncthreads();
-        bitonic_desc<NT>(keys, np2);
-        // probabilities and exclusive prefix mass (block scan in double)
-        double* pm = reinterpret_cast<double*>(gath);  // reuse: own gather list already copied
-        __syncthreads();
-        const float Sf = rs.Sf;
-        const double Sd = rs.S;
-        // each thread handles a contiguous chunk of the sorted keys
-        const int per = (n + NT - 1) / NT;
-        const int i0 = threadIdx.x * per;
-        double local = 0.0;
-        for (int i = i0; i < i0 + per && i < n; ++i) {
-          const float x = key_to_float(uint32_t(keys[i] >> 32));
-          local += double(__fdiv_rn(unnorm(x, c1, nM), Sf));
-        }
-        // block exclusive scan of `local`
-        double incl = local;
-        for (int o = 1; o < 32; o <<= 1) {
-          const double v = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += v;
-        }
-        double* wsum = reinterpret_cast<double*>(ms.wF);
-        if (lane == 31) wsum[warp] = incl;
-        __syncthreads();
-        double woff = 0.0;
-        for (int w = 0; w < warp; ++w) woff += wsum[w];
-        double run = woff + incl - local;
-        // kept prefix: excl(i) <= top_p and i < k; count kept in each chunk
-        int kept = 0;
-        for (int i = i0; i < i0 + per && i < n; ++i) {
-          const float x = key_to_float(uint32_t(keys[i] >> 32));
-          const double pv = double(__fdiv_rn(unnorm(x, c1, nM), Sf));
-          const bool ok = (!p_on || run <= double(tp)) && (!k_on || i < kk);
-          if (!ok) break;
-          ++kept;
-          run += pv;
-        }
-        (void)pm; (void)Sd;
-        // n_K = number of leading kept (kept set is a prefix; chunks are contiguous)
-        __syncthreads();
-        int* kc = reinterpret_cast<int*>(ms.wcnt);
-        // first chunk that is not complete decides the prefix
-        const bool complete = kept == max(0, min(per, n - i0));
-        const unsigned bal = __ballot_sync(0xffffffffu, !complete);
-        if (lane == 0) kc[warp] = bal ? (warp * 32 + ctz_lane(bal)) : 0x7FFFFFFF;
-        __syncthreads();
-        int first_incomplete = 0x7FFFFFFF;
-        for (int w = 0; w < NW; ++w) first_incomplete = min(first_incomplete, kc[w]);
-        __shared__ int s_nk;
-        if (int(threadIdx.x) == first_incomplete) s_nk = i0 + kept;
-        if (threadIdx.x == 0 && first_incomplete == 0x7FFFFFFF) s_nk = n;
-        __syncthreads();
-        const int nK = max(1, min(s_nk, n));
-        // race among the kept tokens
-        const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
-        const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
-        NoiseRoot rt{0.f, 0};
-        int64_t gs = -1;
-        int ms_ = 0;
-        if (!a.noise) {
-          rt = noise_root(key, V);
-          token_group(rt.s, V, &gs, &ms_);
-        }
-        float br = -INFINITY;
-        int bid = 0x7FFFFFFF;
-        for (int i = threadIdx.x; i < nK; i += NT) {
-          const float x = key_to_float(uint32_t(keys[i] >> 32));
-          const int id = int(0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFu));
-          const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
-          const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + id) : tree_noise(key, rt, gs, ms_, id, V);
-          const float r = __fdiv_rn(pv, E);
-          if (rbetter(r, id, br, bid)) { br = r; bid = id; }
-        }
-        for (int o = 16; o; o >>= 1) {
-          const float orr = __shfl_xor_sync(0xffffffffu, br, o);
-          const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-          if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; }
-        }
-        float* wr = reinterpret_cast<float*>(ms.wsfix);
-        int* wi = reinterpret_cast<int*>(ms.wsfix) + NW;
-        if (lane == 0) { wr[warp] = br; wi[warp] = bid; }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
-          a.out_ids[row] = bid == 0x7FFFFFFF ? (nK > 0 ? int(0xFFFFFFFFu - uint32_t(keys[0] & 0xFFFFFFFFu)) : 0) : bid;
-          if (a.out_status) a.out_status[row] = 0;
-        }
+    if (rs.type == kDone) {
+      if (q == 0 && threadIdx.x == 0) {
+        a.out_ids[row] = rs.out;
+        if (a.out_status) a.out_status[row] = rs.status;
       }
       __syncthreads();
       continue;
     }
-
+    if (rs.type == kGather) {
+      if (q == 0) gather_finish<T, CL>(P, row, cluster, data, gath, &share[(ex - 1) & 1], rs, ms);
+      __syncthreads();
+      continue;
+    }
     // kSlow: CTA 0 finishes the row over DSMEM; the peers keep their slices
     // in place until it is done
     if (q == 0) slow_exact<T, CL>(P, row, cluster, data, pen, gath, rs, use_pen, rpv, ms.slow_int);
@@ -1390,6 +1418,11 @@ static int launch_cfg(const KernelArgs& ka, cudaStream_t st, int cap) {
     if (e != cudaSuccess || n <= 0) return set_error(QE_ERR_CUDA, std::string("fused: occupancy query failed: ") + cudaGetErrorString(e));
     max_clusters = n;
     configured_cap = cap;
+    if (const char* dbg = std::getenv("QE_DEBUG")) {
+      if (dbg[0] == '1')
+        std::fprintf(stderr, "[qe] fused: cluster %d x %d threads, %zu B smem/CTA, cap %d, max active clusters %d\n",
+                     CL, NT, smem, cap, n);
+    }
   }
   FusedParams P;
   P.a = ka;

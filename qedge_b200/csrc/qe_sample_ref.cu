@@ -144,18 +144,28 @@ __global__ void __launch_bounds__(256) slice_stats_kernel(KernelArgs a) {
   const float c0 = max_coef(xmax, c1);
   const bool nonfinite = snan || !(xmax > -INFINITY) || !(fabsf(c0) < INFINITY);
   if (!rp.greedy && !nonfinite) {
+    // canonical group sums: relative to each group's own max
     const int64_t ng = slice_groups(L);
+    GroupPart* gp = a.ws.groups + row * a.ws.groups_per_row + slice_group_base(g, V);
     for (int64_t lg = threadIdx.x; lg < ng; lg += blockDim.x) {
-      float fs = 0.f;
+      float gm = -INFINITY;
       for (int m = 0; m < 32; ++m) {
         int64_t o = member_offset(lg, m);
-        if (o < L) fs = __fadd_rn(fs, unnorm(load_x<T>(a, row, s0 + o, smem_bits, s0, rp), c1, c0));
+        if (o < L) gm = fmaxf(gm, load_x<T>(a, row, s0 + o, smem_bits, s0, rp));
       }
-      if (fs > 0.f) atomicAdd(&ssum, (unsigned long long)__double2ull_rn(double(fs) * kSumScale));
+      float fs = 0.f;
+      if (gm > -INFINITY) {
+        const float c0g = max_coef(gm, c1);
+        for (int m = 0; m < 32; ++m) {
+          int64_t o = member_offset(lg, m);
+          if (o < L) fs = __fadd_rn(fs, unnorm(load_x<T>(a, row, s0 + o, smem_bits, s0, rp), c1, c0g));
+        }
+      }
+      gp[lg] = GroupPart{gm, fs};
     }
-    __syncthreads();
-    total = ssum;
   }
+  (void)c0;
+  (void)ssum;
   if (threadIdx.x == 0) {
     part->ymax = xmax;
     part->xbest = xb;
@@ -166,9 +176,9 @@ __global__ void __launch_bounds__(256) slice_stats_kernel(KernelArgs a) {
 }
 
 // --------------------------------------------------------------- kernel 2
-__global__ void row_reduce_kernel(KernelArgs a) {
-  const int64_t row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= a.batch) return;
+__global__ void __launch_bounds__(256) row_reduce_kernel(KernelArgs a) {
+  __shared__ unsigned long long s_sum;
+  const int64_t row = blockIdx.x;
   const RowParams rp = row_params(a, row);
   const SlicePart* sp = a.ws.slices + row * kNumSlices;
   float xb = -INFINITY; int64_t ib = INT64_MAX;
@@ -179,25 +189,39 @@ __global__ void row_reduce_kernel(KernelArgs a) {
     nan |= (sp[g].flags & 1u) != 0;
     M = fmaxf(M, sp[g].ymax);
   }
+  const bool nonfinite_x = nan || !(M > -INFINITY) || M == INFINITY;
+  const float c1 = rp.greedy ? 0.f : temp_coef(rp.T);
+  const float nM = max_coef(M, c1);
+  if (threadIdx.x == 0) s_sum = 0ull;
+  __syncthreads();
+  if (!rp.greedy && !nonfinite_x && fabsf(nM) < INFINITY) {
+    // S = sum over groups of round(2^40 * fsum * 2^(c0_row - c0_group)) * 2^-40
+    const GroupPart* gp = a.ws.groups + row * a.ws.groups_per_row;
+    unsigned long long acc = 0;
+    for (int64_t i = threadIdx.x; i < a.ws.groups_per_row; i += blockDim.x) {
+      const GroupPart g = gp[i];
+      if (g.fsum > 0.f) {
+        const float sc = qe_ex2(__fsub_rn(nM, max_coef(g.gmax, c1)));
+        acc += __double2ull_rn(double(__fmul_rn(g.fsum, sc)) * kSumScale);
+      }
+    }
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&s_sum, acc);
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
   RowInfo* ri = a.ws.rows + row;
   uint32_t status = 0;
   ri->active = 0;
   if (rp.greedy) {
     status = QE_ROW_GREEDY;
-  } else if (nan || !(M > -INFINITY) || M == INFINITY) {
+  } else if (nonfinite_x || !(fabsf(nM) < INFINITY)) {
     status = QE_ROW_NONFINITE;
   } else {
-    const float c1 = temp_coef(rp.T);
-    const float nM = max_coef(M, c1);
-    double S = 0.0;
-    for (int g = 0; g < kNumSlices; ++g) {
-      if ((sp[g].flags & 2u) || !(sp[g].ymax > -INFINITY)) continue;
-      S += double(sp[g].sfix) * (1.0 / kSumScale) * exp2(double(nM) - double(max_coef(sp[g].ymax, c1)));
-    }
+    const double S = double(s_sum) * (1.0 / kSumScale);
     ri->M = nM;
     ri->c1 = c1;
     ri->S = float(S);
-    if (!(fabsf(nM) < INFINITY)) status = QE_ROW_NONFINITE;
     const int64_t V = a.vocab;
     int k = a.top_ks ? a.top_ks[row] : 0;
     bool k_on = k > 0 && int64_t(k) < V;
@@ -459,7 +483,7 @@ static int launch_typed(const KernelArgs& ka, cudaStream_t st) {
   const size_t row_bits = pen ? size_t((V + 31) / 32) * 4 : 0;
   dim3 g1(kNumSlices, unsigned(B));
   slice_stats_kernel<T><<<g1, 256, slice_bits, st>>>(ka);
-  row_reduce_kernel<<<unsigned((B + 127) / 128), 128, 0, st>>>(ka);
+  row_reduce_kernel<<<unsigned(B), 256, 0, st>>>(ka);
   if (!(ka.flags & QE_FLAG_ALL_GREEDY)) {
     threshold_kernel<T><<<unsigned(B), 1024, row_bits, st>>>(ka);
     race_kernel<T><<<g1, 256, slice_bits, st>>>(ka);
