@@ -101,6 +101,58 @@ template <> struct Load8<float> {
   }
 };
 
+// Max of 8 consecutive elements starting at smem element offset `off`
+// (NaN-propagating); elements at or beyond `nvalid` are ignored.  16-bit
+// types use packed max on the raw words, without unpacking.
+template <typename T> struct Max8;
+template <> struct Max8<__nv_bfloat16> {
+  static __device__ __forceinline__ float run(const void* buf, int off, int nvalid) {
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(buf) + off);
+    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    if (nvalid < 8) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (2 * i >= nvalid) ws[i] = 0xFF80FF80u;                 // -inf, -inf
+        else if (2 * i + 1 >= nvalid) ws[i] = (ws[i] & 0xFFFFu) | 0xFF800000u;
+      }
+    }
+    __nv_bfloat162 a = __hmax2_nan(*reinterpret_cast<__nv_bfloat162*>(&ws[0]), *reinterpret_cast<__nv_bfloat162*>(&ws[1]));
+    __nv_bfloat162 b = __hmax2_nan(*reinterpret_cast<__nv_bfloat162*>(&ws[2]), *reinterpret_cast<__nv_bfloat162*>(&ws[3]));
+    a = __hmax2_nan(a, b);
+    const float lo = __bfloat162float(__low2bfloat16(a)), hi = __bfloat162float(__high2bfloat16(a));
+    return (lo != lo || hi != hi) ? NAN : fmaxf(lo, hi);
+  }
+};
+template <> struct Max8<__half> {
+  static __device__ __forceinline__ float run(const void* buf, int off, int nvalid) {
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(buf) + off);
+    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    if (nvalid < 8) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (2 * i >= nvalid) ws[i] = 0xFC00FC00u;
+        else if (2 * i + 1 >= nvalid) ws[i] = (ws[i] & 0xFFFFu) | 0xFC000000u;
+      }
+    }
+    __half2 a = __hmax2_nan(*reinterpret_cast<__half2*>(&ws[0]), *reinterpret_cast<__half2*>(&ws[1]));
+    __half2 b = __hmax2_nan(*reinterpret_cast<__half2*>(&ws[2]), *reinterpret_cast<__half2*>(&ws[3]));
+    a = __hmax2_nan(a, b);
+    const float lo = __low2float(a), hi = __high2float(a);
+    return (lo != lo || hi != hi) ? NAN : fmaxf(lo, hi);
+  }
+};
+template <> struct Max8<float> {
+  static __device__ __forceinline__ float run(const void* buf, int off, int nvalid) {
+    float x[8];
+    Load8<float>::run(buf, off, nvalid, x);
+    float m = x[0];
+    bool nan = x[0] != x[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) { m = fmaxf(m, x[i]); nan |= x[i] != x[i]; }
+    return nan ? NAN : m;
+  }
+};
+
 // Apply the repetition penalty to the elements whose bit is set in `bits8`.
 __device__ __forceinline__ void apply_penalty8(uint32_t bits8, float rp, float x[8]) {
   if (bits8) {

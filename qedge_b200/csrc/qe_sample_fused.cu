@@ -152,30 +152,40 @@ __device__ __forceinline__ void list_insert(Cand* l, int n, const Cand& c) {
   l[i] = c;
 }
 
-// Warp-level: merge the 32 lanes' (r, x, E, id) into the warp list (lane 0
-// owns the list in shared memory).  At most n rounds.
+// Warp-level: merge the 32 lanes' (r, x, E, id) into the warp's sorted list
+// of n candidates (lane 0 owns the list in shared memory).  A warp-wide max
+// first rejects the common case where no lane can enter the list; otherwise
+// each round extracts the best remaining lane through one 64-bit key
+// (ordered ratio, inverted id) per shuffle step.
 __device__ __forceinline__ void warp_merge(Cand* wl, int n, float r, float x, float E, int id) {
   const int lane = threadIdx.x & 31;
+  float m = r;
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float floor_r = wl[n - 1].r;
+  if (!(m >= floor_r) || !(m > -INFINITY)) return;
+  unsigned long long key = r > -INFINITY
+      ? (uint64_t(ordered_key(r)) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(id)) : 0ull;
   for (int round = 0; round < n; ++round) {
-    float br = r; int bid = id; int bl = lane;
+    unsigned long long best = key;
     for (int o = 16; o; o >>= 1) {
-      float orr = __shfl_xor_sync(0xffffffffu, br, o);
-      int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-      int ol = __shfl_xor_sync(0xffffffffu, bl, o);
-      if (rbetter(orr, oid, br, bid) || (!rbetter(br, bid, orr, oid) && ol < bl)) { br = orr; bid = oid; bl = ol; }
+      const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+      best = ok > best ? ok : best;
     }
-    if (!(br > -INFINITY)) break;
+    if (best == 0ull) break;
+    const int bl = __ffs(__ballot_sync(0xffffffffu, key == best)) - 1;
+    const float br = __shfl_sync(0xffffffffu, r, bl);
     const float bx = __shfl_sync(0xffffffffu, x, bl);
     const float bE = __shfl_sync(0xffffffffu, E, bl);
-    bool full_and_worse = false;
+    const int bid = __shfl_sync(0xffffffffu, id, bl);
+    bool stop = false;
     if (lane == 0) {
-      full_and_worse = !rbetter(br, bid, wl[n - 1].r, wl[n - 1].id);
-      if (!full_and_worse) list_insert(wl, n, Cand{br, bx, bE, bid});
+      stop = !rbetter(br, bid, wl[n - 1].r, wl[n - 1].id);
+      if (!stop) list_insert(wl, n, Cand{br, bx, bE, bid});
     }
-    full_and_worse = __shfl_sync(0xffffffffu, full_and_worse, 0);
+    stop = __shfl_sync(0xffffffffu, stop, 0);
     __syncwarp();
-    if (full_and_worse) break;
-    if (lane == bl) r = -INFINITY;
+    if (stop) break;
+    if (lane == bl) key = 0ull;
   }
 }
 
@@ -307,123 +317,180 @@ __device__ void bitonic_desc(unsigned long long* k, int n) {
 }
 
 
-// Exact finish of one row by CTA 0 alone, reading every CTA's slice over
-// DSMEM (the peers wait at a cluster barrier meanwhile).  The kept set is
-// found by radix selection on the ordered logit keys, with integer counts
-// (top-k) and probability masses in 2^-62 fixed point (top-p), as in the
-// multi-kernel path; then the race runs over the kept ids in id order.
+// Exact finish of one row by the whole cluster, each CTA working on its own
+// slice: the kept set is found by radix selection on the ordered logit keys
+// (4 passes of 8 bits; per-CTA shared-memory histograms of counts and of
+// probability mass in 2^-40 fixed point, merged over DSMEM), ties at the
+// boundary are kept in id order, and the race runs over every kept token.
+// Used when the race candidates all fall outside the kept set and the kept
+// set is too large to gather.  Every CTA calls it (cluster barriers inside).
 template <typename T, int CL>
-__device__ void slow_exact(const FusedParams& P, int64_t row, cg::cluster_group& cluster, void* data,
-                           uint32_t* pen, unsigned long long* scratch, const RowState& rs, bool use_pen,
-                           float rpv, int* s_int) {
-  constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
+__device__ __noinline__ void cluster_exact(const FusedParams& P, int64_t row, cg::cluster_group& cluster,
+                                           const void* data, const uint32_t* pen, unsigned long long* scratch,
+                                           const RowState& rs, bool use_pen, float rpv, int64_t cta_start,
+                                           int n_cta, int* s_int, float* s_flt) {
+  constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW;
   const KernelArgs& a = P.a;
   const int64_t V = a.vocab;
-  const float c1 = rs.c1, nM = rs.nM, Sf = rs.Sf;
-  uint32_t* hc = reinterpret_cast<uint32_t*>(scratch);
-  unsigned long long* hm = scratch + 128;  // 256 u64 after 256 u32
-  int& s_bin = s_int[0];
-  long long* s_ll = reinterpret_cast<long long*>(s_int + 2);  // [0] cbase [1] mbase
-  uint32_t* s_u = reinterpret_cast<uint32_t*>(s_int + 8);     // [0] prefix [1] mask
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float c1 = rs.c1, nM = rs.nM, Sf = rs.Sf;
+  uint32_t* hc = reinterpret_cast<uint32_t*>(scratch);                // [256]
+  unsigned long long* hm = scratch + 128;                              // [256]
+  long long* pub = reinterpret_cast<long long*>(scratch + 384);        // published scalars [8]
+  const int q = int(cluster.block_rank());
+  const unsigned long long Sfix = __double2ull_rn(rs.S * kSumScale);
+  auto fixe = [&](float x) { return (unsigned long long)__double2ull_rn(double(unnorm(x, c1, nM)) * kSumScale); };
 
-  auto for_all = [&](auto&& f) {
-    for (int r = 0; r < CL; ++r) {
-      const int64_t s0 = slice_start(r * U, V), s1 = slice_start(r * U + U, V);
-      const void* d = cluster.map_shared_rank(data, r);
-      const uint32_t* pb = cluster.map_shared_rank(pen, r);
-      for (int off = threadIdx.x; off < int(s1 - s0); off += NT) f(s0 + off, load1<T>(d, pb, use_pen, rpv, off));
-    }
-  };
-  auto prob = [&](float x) { return __fdiv_rn(unnorm(x, c1, nM), Sf); };
-
-  // radix select: weighted (top-p) or counting (top-k)
-  auto select = [&](bool weighted, unsigned long long Tfix, long long pos, uint32_t& key_out, long long& keep_out) {
-    if (threadIdx.x == 0) { s_u[0] = 0; s_u[1] = 0; s_ll[0] = 0; s_ll[1] = 0; }
-    __syncthreads();
+  uint32_t prefix = 0, msk = 0;
+  long long cbase = 0;
+  unsigned long long mbase = 0;
+  // radix selection: weighted (top-p: last token whose exclusive mass <= T)
+  // or counting (top-k: the token at position `pos`); sets the boundary key
+  // in `prefix`, the tokens strictly above it in `cbase`, the kept count
+  auto select = [&](bool weighted, unsigned long long Tfix, long long pos, long long& keep) {
+    prefix = 0; msk = 0; cbase = 0; mbase = 0;
+    long long nt = 0;
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = threadIdx.x; b < 256; b += NT) { hc[b] = 0; hm[b] = 0; }
       __syncthreads();
-      const uint32_t pre = s_u[0], msk = s_u[1];
-      for_all([&](int64_t, float x) {
+      for (int off = threadIdx.x; off < n_cta; off += NT) {
+        const float x = load1<T>(data, pen, use_pen, rpv, off);
         const uint32_t kq = ordered_key(x);
-        if ((kq & msk) == pre) {
+        if ((kq & msk) == prefix) {
           const int b = (kq >> shift) & 255;
           atomicAdd(&hc[b], 1u);
-          if (weighted) atomicAdd(&hm[b], (unsigned long long)__double2ull_rn(double(prob(x)) * kMassScale));
+          if (weighted && x > -INFINITY) atomicAdd(&hm[b], fixe(x));
         }
-      });
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        long long c = s_ll[0];
-        unsigned long long m = (unsigned long long)s_ll[1];
-        int cand = -1;
-        long long cc = c;
-        unsigned long long cm = m;
-        for (int b = 255; b >= 0; --b) {
-          if (hc[b] == 0) continue;
-          if (weighted) {
-            if (m <= Tfix) { cand = b; cc = c; cm = m; } else break;
-          } else {
-            if (pos < c + (long long)hc[b]) { cand = b; cc = c; break; }
+      }
+      cluster.sync();
+      if (warp == 0) {
+        // lane l holds bins 255-8l .. 248-8l (descending key order)
+        uint32_t c8[8];
+        unsigned long long m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { c8[i] = 0; m8[i] = 0; }
+        for (int r = 0; r < CL; ++r) {
+          const uint32_t* rc = cluster.map_shared_rank(hc, r);
+          const unsigned long long* rm = cluster.map_shared_rank(hm, r);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int b = 255 - (lane * 8 + i);
+            c8[i] += rc[b];
+            if (weighted) m8[i] += rm[b];
           }
-          m += hm[b];
-          c += hc[b];
         }
-        if (cand < 0) cand = 0;
-        s_bin = cand;
-        s_u[0] = pre | (uint32_t(cand) << shift);
-        s_u[1] = msk | (255u << shift);
-        s_ll[0] = cc;
-        s_ll[1] = (long long)cm;
+        long long lc = 0;
+        unsigned long long lm = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { lc += c8[i]; lm += m8[i]; }
+        long long ic = lc;
+        unsigned long long im = lm;
+        for (int o = 1; o < 32; o <<= 1) {
+          const long long vc = __shfl_up_sync(0xffffffffu, ic, o);
+          const unsigned long long vm = __shfl_up_sync(0xffffffffu, im, o);
+          if (lane >= o) { ic += vc; im += vm; }
+        }
+        long long c = cbase + ic - lc;
+        unsigned long long m = mbase + im - lm;
+        int cand = -1;
+        long long cc = 0, ct = 0;
+        unsigned long long cm = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (c8[i]) {
+            if (weighted) {
+              if (m <= Tfix) { cand = 255 - (lane * 8 + i); cc = c; cm = m; ct = c8[i]; }
+            } else if (pos >= c && pos < c + (long long)c8[i]) {
+              cand = 255 - (lane * 8 + i); cc = c; cm = m; ct = c8[i];
+            }
+          }
+          c += c8[i];
+          m += m8[i];
+        }
+        int pick = cand;
+        for (int o = 16; o; o >>= 1) {
+          const int other = __shfl_xor_sync(0xffffffffu, pick, o);
+          if (other >= 0 && (pick < 0 || (weighted ? other < pick : true))) pick = other;
+        }
+        if (pick < 0) pick = 0;
+        const unsigned who = __ballot_sync(0xffffffffu, cand == pick);
+        const int wl_ = who ? __ffs(who) - 1 : 0;
+        cc = __shfl_sync(0xffffffffu, cc, wl_);
+        cm = __shfl_sync(0xffffffffu, cm, wl_);
+        ct = __shfl_sync(0xffffffffu, ct, wl_);
+        if (lane == 0) { pub[0] = pick; pub[1] = cc; pub[2] = (long long)cm; pub[3] = ct; }
       }
       __syncthreads();
+      prefix |= uint32_t(pub[0]) << shift;
+      msk |= 255u << shift;
+      cbase = pub[1];
+      mbase = (unsigned long long)pub[2];
+      nt = pub[3];
+      cluster.sync();  // peers are done reading this CTA's histogram
     }
-    key_out = s_u[0];
-    const long long nt = hc[s_bin & 255];
     if (weighted) {
-      const unsigned long long f = __double2ull_rn(double(prob(key_to_float(key_out))) * kMassScale);
+      const unsigned long long f = fixe(key_to_float(prefix));
       long long c = nt;
       if (f > 0) {
-        const unsigned long long room = Tfix - (unsigned long long)s_ll[1];
-        const unsigned long long qq = room / f + 1;
+        const unsigned long long qq = (Tfix - mbase) / f + 1;
         if (qq < (unsigned long long)nt) c = (long long)qq;
       }
-      keep_out = s_ll[0] + c;  // number of kept tokens
+      keep = cbase + c;
     } else {
-      keep_out = pos + 1;
+      keep = pos + 1;
     }
-    __syncthreads();
   };
 
   long long n_keep = V;
   uint32_t vkey = 0;
   bool have = false;
+  long long above = 0;
   if (rs.p_on) {
-    const unsigned long long Tfix = (unsigned long long)(double(rs.tp) * kMassScale);
-    select(true, Tfix, 0, vkey, n_keep);
-    have = true;
+    select(true, (unsigned long long)(double(rs.tp) * double(Sfix)), 0, n_keep);
+    vkey = prefix; above = cbase; have = true;
   }
   if (rs.k_on && rs.k < n_keep) {
-    select(false, 0ull, rs.k - 1, vkey, n_keep);
-    have = true;
+    select(false, 0ull, rs.k - 1, n_keep);
+    vkey = prefix; above = cbase; have = true;
   }
-  // tokens strictly above vkey are kept; ties at vkey are kept in id order
-  // until n_keep tokens are kept
-  long long above = 0;
-  if (have) {
-    if (threadIdx.x == 0) s_ll[0] = 0;
-    __syncthreads();
-    long long cnt = 0;
-    for_all([&](int64_t, float x) { cnt += ordered_key(x) > vkey; });
-    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&s_ll[0]), (unsigned long long)cnt);
-    __syncthreads();
-    above = s_ll[0];
-    __syncthreads();
+  const long long tie_keep = n_keep - above;
+  // id of the last kept tie: tie counts per CTA (id order = CTA order, then
+  // offset order), the CTA that holds it finds it with a block scan
+  const int per = (n_cta + NT - 1) / NT;
+  const int i0 = threadIdx.x * per;
+  int myties = 0;
+  for (int i = i0; i < i0 + per && i < n_cta; ++i) myties += ordered_key(load1<T>(data, pen, use_pen, rpv, i)) == vkey;
+  int incl = myties;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
   }
-  const long long tie_keep = have ? n_keep - above : 0;
-  // race over the kept ids in id order (tie rank by a running block scan)
+  if (lane == 31) s_int[warp] = incl;
+  __syncthreads();
+  int woff = 0, ctaties = 0;
+  for (int w = 0; w < NW; ++w) { if (w < warp) woff += s_int[w]; ctaties += s_int[w]; }
+  if (threadIdx.x == 0) pub[4] = ctaties;
+  cluster.sync();
+  long long before_cta = 0;
+  for (int r = 0; r < q; ++r) before_cta += cluster.map_shared_rank(pub, r)[4];
+  {
+    long long rank = before_cta + woff + incl - myties;
+    for (int i = i0; i < i0 + per && i < n_cta; ++i) {
+      if (ordered_key(load1<T>(data, pen, use_pen, rpv, i)) == vkey) {
+        if (rank == tie_keep - 1) pub[5] = cta_start + i;
+        ++rank;
+      }
+    }
+  }
+  if (threadIdx.x == 0 && !(tie_keep - 1 >= before_cta && tie_keep - 1 < before_cta + ctaties)) pub[5] = -1;
+  cluster.sync();
+  long long id_c = 0x7FFFFFFFll;
+  for (int r = 0; r < CL; ++r) {
+    const long long v = cluster.map_shared_rank(pub, r)[5];
+    if (v >= 0) id_c = v;
+  }
+  if (!have) id_c = 0x7FFFFFFFll;
+  // race over the kept tokens of this slice
   const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
   const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
   NoiseRoot rt{0.f, 0};
@@ -433,36 +500,18 @@ __device__ void slow_exact(const FusedParams& P, int64_t row, cg::cluster_group&
     rt = noise_root(key, V);
     token_group(rt.s, V, &gs, &mem_s);
   }
-  int* wt = s_int + 16;  // per-warp tie counts
-  long long tie_base = 0;
   float br = -INFINITY;
   int bid = 0x7FFFFFFF;
-  for (int r = 0; r < CL; ++r) {
-    const int64_t s0 = slice_start(r * U, V), s1 = slice_start(r * U + U, V);
-    const void* d = cluster.map_shared_rank(data, r);
-    const uint32_t* pb = cluster.map_shared_rank(pen, r);
-    for (int base = 0; base < int(s1 - s0); base += NT) {
-      const int off = base + threadIdx.x;
-      const bool valid = off < int(s1 - s0);
-      const float x = valid ? load1<T>(d, pb, use_pen, rpv, off) : -INFINITY;
-      const uint32_t kq = ordered_key(x);
-      const bool tie = have && valid && kq == vkey;
-      const uint32_t bal = __ballot_sync(0xffffffffu, tie);
-      if (lane == 0) wt[warp] = __popc(bal);
-      __syncthreads();
-      int before = 0, total = 0;
-      for (int w = 0; w < NW; ++w) { if (w < warp) before += wt[w]; total += wt[w]; }
-      const long long trank = tie_base + before + __popc(bal & ((1u << lane) - 1u));
-      const bool in = valid && (!have || kq > vkey || (tie && trank < tie_keep));
-      if (in) {
-        const int64_t j = s0 + off;
-        const float pv = prob(x);
-        const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + j) : tree_noise(key, rt, gs, mem_s, j, V);
-        const float rv = __fdiv_rn(pv, E);
-        if (rbetter(rv, int(j), br, bid)) { br = rv; bid = int(j); }
-      }
-      tie_base += total;
-      __syncthreads();
+  for (int off = threadIdx.x; off < n_cta; off += NT) {
+    const float x = load1<T>(data, pen, use_pen, rpv, off);
+    const uint32_t kq = ordered_key(x);
+    const int64_t j = cta_start + off;
+    const bool in = !have || kq > vkey || (kq == vkey && j <= id_c);
+    if (in && x > -INFINITY) {
+      const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
+      const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + j) : tree_noise(key, rt, gs, mem_s, j, V);
+      const float rv = __fdiv_rn(pv, E);
+      if (rbetter(rv, int(j), br, bid)) { br = rv; bid = int(j); }
     }
   }
   for (int o = 16; o; o >>= 1) {
@@ -470,18 +519,27 @@ __device__ void slow_exact(const FusedParams& P, int64_t row, cg::cluster_group&
     const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
     if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; }
   }
-  float* wr = reinterpret_cast<float*>(hm);
-  int* wi = reinterpret_cast<int*>(hm) + NW;
-  if (lane == 0) { wr[warp] = br; wi[warp] = bid; }
+  __syncthreads();
+  if (lane == 0) { s_flt[warp] = br; s_int[warp] = bid; }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < NW; ++w) if (rbetter(wr[w], wi[w], br, bid)) { br = wr[w]; bid = wi[w]; }
+    for (int w = 1; w < NW; ++w) if (rbetter(s_flt[w], s_int[w], br, bid)) { br = s_flt[w]; bid = s_int[w]; }
+    reinterpret_cast<float*>(pub + 6)[0] = br;
+    pub[7] = bid;
+  }
+  cluster.sync();
+  if (q == 0 && threadIdx.x == 0) {
+    for (int r = 0; r < CL; ++r) {
+      const long long* pr = cluster.map_shared_rank(pub, r);
+      const float rr = reinterpret_cast<const float*>(pr + 6)[0];
+      const int ri = int(pr[7]);
+      if (rbetter(rr, ri, br, bid)) { br = rr; bid = ri; }
+    }
     a.out_ids[row] = bid == 0x7FFFFFFF ? rs.out : bid;
     if (a.out_status) a.out_status[row] = QE_ROW_SLOW;
   }
-  __syncthreads();
+  cluster.sync();  // peers keep their published scalars until CTA 0 has read them
 }
-
 
 // CTA 0 finishes a row from the keys every CTA gathered (all tokens with
 // x' >= L, which provably contains the kept set): sort, exclusive prefix
@@ -718,11 +776,18 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
               const int nv = un.L - local;
               if (nv > 0) {
                 const int off = un.uoff + local;
-                float x[8];
-                Load8<T>::run(data, off, nv, x);
-                if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+                const uint32_t pb = use_pen ? ((pen[off >> 5] >> (off & 31)) & 0xFFu) : 0u;
+                if (pb) {
+                  float x[8];
+                  Load8<T>::run(data, off, nv, x);
+                  apply_penalty8(pb, rpv, x);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) { m = fmaxf(m, x[i]); lnan |= (x[i] != x[i]); }
+                  for (int i = 0; i < 8; ++i) { m = fmaxf(m, x[i]); lnan |= (x[i] != x[i]); }
+                } else {
+                  const float mb = Max8<T>::run(data, off, nv);
+                  lnan |= (mb != mb);
+                  m = fmaxf(m, mb);
+                }
                 if (parity && need_race) {
                   const float* nz = a.noise + row * a.noise_ld + geo.cta_start + off;
                   if (P.noise_vec && nv >= 8) {
@@ -844,7 +909,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     }
 
     // ------------------------------------------------------------ race (local, CTA scale)
-    const int Rr = !(p_on || k_on) ? 1 : ((p_on && !k_on && tp >= 0.9f) ? 2 : 4);
+    const int Rr = !(p_on || k_on) ? 1 : ((p_on && !k_on && tp >= 0.99f) ? 2 : kMaxR);
     float bnd[kSlots];
     uint32_t uw[kSlots], sw[kSlots];
     unsigned done_mask = 0;
@@ -1382,10 +1447,9 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
       __syncthreads();
       continue;
     }
-    // kSlow: CTA 0 finishes the row over DSMEM; the peers keep their slices
-    // in place until it is done
-    if (q == 0) slow_exact<T, CL>(P, row, cluster, data, pen, gath, rs, use_pen, rpv, ms.slow_int);
-    cluster.sync();
+    // kSlow: the cluster finishes the row exactly, each CTA on its own slice
+    cluster_exact<T, CL>(P, row, cluster, data, pen, gath, rs, use_pen, rpv, geo.cta_start, n_cta,
+                         ms.slow_int, ms.wb);
   }
   // do not leave while peers may still read this CTA's shared memory
   cluster.sync();

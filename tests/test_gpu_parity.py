@@ -147,3 +147,20 @@ def test_row_offset_keys_global_rows(sampler):
     full = sampler(lg, t, p, use_top_p=True, seed=4, step=0)
     half = sampler(lg[4:], t[4:], p[4:], use_top_p=True, seed=4, step=0, row_offset=4)
     np.testing.assert_array_equal(full[4:].cpu().numpy(), half.cpu().numpy())
+
+
+def test_fallback_paths_vs_oracle(sampler):
+    """Flat logits with a small nucleus: the race candidates often fall
+    outside the kept set, so rows finish through the gather and the
+    cluster-wide exact paths (reported in out_status); ids must still match
+    the oracle."""
+    g = np.random.Generator(np.random.PCG64(77))
+    B, V = 24, 248_320
+    x = g.standard_normal((B, V), dtype=np.float32) * np.float32(0.3)
+    w = W.Workload("flat", W.to_bf16_bits(x), "bf16", np.ones(B, np.float32),
+                   np.array([0.05, 0.3, 0.6] * 8, np.float32), np.zeros(B, np.int32),
+                   np.ones(B, np.float32), None, None, use_top_p=True)
+    st = torch.zeros(B, dtype=torch.int32, device="cuda")
+    ids = run(sampler, w, None, seed=9, step=2, out_status=st)
+    noise = ON.philox_noise(B, V, 9, 2)
+    np.testing.assert_array_equal(ids, oracle_ids(w, noise))
