@@ -94,6 +94,25 @@ int qe_sample(const qe_sample_args* args, void* stream);
 /* Message of the last error returned on this thread ("" if none). */
 const char* qe_last_error(void);
 
+/* Bytes of the scratch array built into the library for qe_sample_noalloc. */
+#define QE_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* qe_sample without a caller workspace (it has no counterpart in the
+ * reference).  For callers that cannot allocate device memory: plugins inside
+ * a host engine that owns every device allocation, language bindings with no
+ * device-memory API.  Same kernels and results as qe_sample; the scratch
+ * comes from one QE_NOALLOC_SCRATCH_BYTES array inside the library, which
+ * every GPU that uses the library holds until the process exits.
+ * `workspace` and `workspace_bytes` in args are ignored.  Calls whose
+ * qe_sample_workspace_size(batch, vocab) exceeds the array are rejected with
+ * QE_ERR_UNSUPPORTED (at V = 248,320 about 500 rows fit).  The first call on
+ * a device looks up the array's device address; make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (other streams, other host threads) race and must be serialised by
+ * the caller.  No part of the array needs to start at zero: every kernel
+ * writes the scratch it reads first.  Allocates nothing. */
+int qe_sample_noalloc(const qe_sample_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

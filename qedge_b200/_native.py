@@ -19,7 +19,9 @@ STATUS_NAMES = {0: "QE_OK", -1: "QE_ERR_INVALID", -2: "QE_ERR_CUDA",
                 -3: "QE_ERR_WORKSPACE", -4: "QE_ERR_UNSUPPORTED"}
 
 # Every symbol the header declares; tests check the library exports them.
-EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error")
+EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error",
+            "qe_sample_noalloc")
+QE_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _vp = ctypes.c_void_p
 
@@ -79,6 +81,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
         lib.qe_sample_workspace_size.argtypes = [ctypes.c_int64, ctypes.c_int64]
         lib.qe_sample.restype = ctypes.c_int
         lib.qe_sample.argtypes = [ctypes.POINTER(QeSampleArgs), _vp]
+        lib.qe_sample_noalloc.restype = ctypes.c_int
+        lib.qe_sample_noalloc.argtypes = [ctypes.POINTER(QeSampleArgs), _vp]
         lib.qe_last_error.restype = ctypes.c_char_p
         lib.qe_last_error.argtypes = []
         ver = lib.qe_abi_version()
