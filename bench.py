@@ -225,14 +225,14 @@ def main():
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.e2e_steps):
+    for i in range(max(args.e2e_steps, 1)):
         dbuf.copy_(host, non_blocking=True)
         ids = sampler(dbuf, temps, tps, use_top_p=w.use_top_p, step=10_000 + i,
                       row_offset=row_offset, noise=noise, **kw)
         out_host.copy_(ids, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    e2e_ms = e0.elapsed_time(e1) / max(args.e2e_steps, 1)
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -14,19 +14,20 @@ has no per-request seed.  The B200 path keys its noise on
 function from that paper).  Known-answer vectors from the Random123
 distribution pin :func:`philox4x32_10` (see ``tests/test_oracle_noise.py``).
 
-The Exp(1) noise tensor ``E[B, V]`` is defined as a two-level
-"minimum-first" tree, which gives i.i.d. Exp(1) marginals and lets the GPU
-kernel skip generating noise for tokens that cannot win the race:
+The Exp(1) noise tensor ``E[B, V]`` is defined as a "minimum-first" tree,
+which gives i.i.d. Exp(1) marginals and lets the GPU kernel skip generating
+noise for tokens that cannot win the race:
 
 * root (one per row): ``E_root = -ln(u_root) / V``; a uniformly chosen token
   ``s`` carries that minimum;
-* group ``G`` (32 tokens, layout below): ``E_min(G) = E_root`` if ``s`` is in
-  ``G`` (and ``s`` is its argmin); otherwise
-  ``E_min(G) = E_root + (-ln(u_G)) / n_G`` and a uniformly chosen member
-  carries it.  The two groups of a tile pair (tiles 2q and 2q+1, same lane)
-  share one Philox call: words (x, y) for the even tile, (z, w) for the odd
-  one (first word -> u_G, second -> member selector);
-* every other token ``j`` of ``G``: ``E_j = E_min(G) + (-ln(u_j))``.
+* group ``G`` (up to 32 tokens, layout below), one Philox call whose counter
+  is the global group id, words ``(x, y, z, w)``:
+  ``E_min(G) = E_root + (-ln(u_x)) / n_G`` carried by member
+  ``select(y, n_G)`` -- or ``E_root`` carried by ``s`` if ``s`` is in ``G``;
+  then the second smallest value ``E2(G) = E_min(G) + (-ln(u_z)) / (n_G - 1)``
+  carried by member ``select(w, n_G - 1)`` counted among the members other
+  than the argmin;
+* every other token ``j`` of ``G``: ``E_j = E2(G) + (-ln(u_j))``.
 
 By the memoryless property of the exponential distribution this is exactly
 the joint law of ``V`` i.i.d. Exp(1) variables.  All arithmetic below is
@@ -135,8 +136,8 @@ def slice_starts(V: int) -> np.ndarray:
 
 
 def group_layout(V: int):
-    """For every token id return (global group id, member index), the member
-    count of every group and every group's Philox (counter index, word pair).
+    """For every token id return (global group id, member index) and the
+    member count of every group.
 
     Inside slice g (ids [start, end)), the local offset o = j - start splits
     as tile t = o >> 10, block b = (o >> 8) & 3, lane l = (o >> 3) & 31,
@@ -147,9 +148,7 @@ def group_layout(V: int):
     gid = np.empty(V, dtype=np.int64)
     mem = np.empty(V, dtype=np.int64)
     sizes = []
-    ctrs = []
     base = 0
-    pair_base = 0
     for g in range(NSLICE):
         a, z = int(starts[g]), int(starts[g + 1])
         L = z - a
@@ -163,13 +162,9 @@ def group_layout(V: int):
         mem[a:z] = b * 8 + i
         cnt = np.bincount(t * GROUP_LANES + lane, minlength=ntiles * GROUP_LANES)
         sizes.append(cnt)
-        gt = np.arange(ntiles * GROUP_LANES, dtype=np.int64)
-        ctrs.append(np.stack([pair_base + (gt >> 6) * GROUP_LANES + (gt & 31), (gt >> 5) & 1], axis=1))
         base += ntiles * GROUP_LANES
-        pair_base += ((ntiles + 1) // 2) * GROUP_LANES
     sizes = np.concatenate(sizes) if sizes else np.zeros(0, np.int64)
-    ctrs = np.concatenate(ctrs) if ctrs else np.zeros((0, 2), np.int64)
-    return gid, mem, sizes.astype(np.int64), ctrs
+    return gid, mem, sizes.astype(np.int64)
 
 
 def _select(w1, w2, n):
@@ -193,31 +188,40 @@ def philox_noise(B: int, V: int, seed: int, step: int, row_offset: int = 0) -> n
     k0, k1 = seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF
     s_lo = step & 0xFFFFFFFF
     hi = ((step >> 32) << 2) & 0xFFFFFFFF
-    gid, mem, sizes, ctrs = group_layout(V)
+    gid, mem, sizes = group_layout(V)
     NG = sizes.shape[0]
     Vf = np.float32(V)
     out = np.empty((B, V), dtype=np.float32)
     jarange = np.arange(V, dtype=np.int64)
+    garange = np.arange(NG, dtype=np.int64)
+    n = np.maximum(sizes, 1)
+    nf = n.astype(np.float32)
+    n1f = np.maximum(n - 1, 1).astype(np.float32)
     for r in range(B):
         row = row_offset + r
         w = philox4x32_10(0, row, s_lo, hi | TAG_ROOT, k0, k1)
         e_root = (neglog_f32(uniform_open(w[0])) / Vf).astype(np.float32)
         s = int(_select(w[1], w[2], V))
-        wg = philox4x32_10(ctrs[:, 0], row, s_lo, hi | TAG_GROUP, k0, k1)
-        odd = ctrs[:, 1] == 1
-        w_u = np.where(odd, wg[2], wg[0])
-        w_s = np.where(odd, wg[3], wg[1])
-        ng = np.maximum(sizes, 1).astype(np.float32)
-        e_min = (e_root + (neglog_f32(uniform_open(w_u)) / ng).astype(np.float32)).astype(np.float32)
-        arg = _select32(w_s, np.maximum(sizes, 1))
+        wg = philox4x32_10(garange, row, s_lo, hi | TAG_GROUP, k0, k1)
+        e_min = (e_root + (neglog_f32(uniform_open(wg[0])) / nf).astype(np.float32)).astype(np.float32)
+        arg = _select32(wg[1], n)
         gs = gid[s]
         e_min[gs] = e_root
         arg[gs] = mem[s]
+        e2 = (e_min + (neglog_f32(uniform_open(wg[2])) / n1f).astype(np.float32)).astype(np.float32)
+        i2 = _select32(wg[3], np.maximum(n - 1, 1))
+        arg2 = np.where(i2 < arg, i2, i2 + 1)
+        single = n < 2
+        e2[single] = np.inf
+        arg2[single] = -1
         wt = philox4x32_10(jarange >> 2, row, s_lo, hi | TAG_TOKEN, k0, k1)
         wsel = np.choose((jarange & 3).astype(np.int64), wt)
-        emin_j = e_min[gid]
-        e = (emin_j + neglog_f32(uniform_open(wsel))).astype(np.float32)
+        e2_j = e2[gid]
+        with np.errstate(invalid="ignore"):
+            e = (e2_j + neglog_f32(uniform_open(wsel))).astype(np.float32)
+        is2 = mem == arg2[gid]
+        e[is2] = e2_j[is2]
         is_arg = mem == arg[gid]
-        e[is_arg] = emin_j[is_arg]
+        e[is_arg] = e_min[gid][is_arg]
         out[r] = e
     return out

@@ -82,8 +82,11 @@ __device__ __forceinline__ float qe_exp(float d) {
 }
 
 // Repetition penalty of one logit (Hugging Face rule: x<0 ? x*rp : x/rp).
+// Out-of-line IEEE division: keeps the rarely taken penalty branch small at
+// every call site.
+static __device__ __noinline__ float div_rn_outlined(float x, float y) { return __fdiv_rn(x, y); }
 __device__ __forceinline__ float penalise(float x, float rp) {
-  return x < 0.f ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
+  return x < 0.f ? __fmul_rn(x, rp) : div_rn_outlined(x, rp);
 }
 
 // Greedy comparison of torch.argmax: NaN is maximal, first index wins ties.
@@ -174,30 +177,45 @@ __device__ __forceinline__ NoiseRoot noise_root(const NoiseKey& k, int64_t V) {
   r.s = select_index(w.y, w.z, uint32_t(V));
   return r;
 }
-// Minimum of a group and the member index that carries it.  The two groups
-// of a tile pair share one Philox call (counter `ctr`): words (x, y) for the
-// even tile, (z, w) for the odd one.
-struct GroupMin { float e_min; int arg; };
-__device__ __forceinline__ GroupMin group_min_from(const NoiseRoot& root, uint32_t wu, uint32_t ws, int n) {
-  GroupMin g;
-  g.e_min = __fadd_rn(root.e_root, __fdiv_rn(neglog(uniform_open(wu)), float(n)));
-  g.arg = int(select_index32(ws, uint32_t(n)));
+// Noise of a group of n members (one Philox call, counter = global group
+// id): its minimum E_min and the member carrying it, then the gap to the
+// second smallest value, E2 = E_min + (-ln u')/(n-1), and the member
+// carrying that (uniform among the others).  Every other member j has
+// E_j = E2 + (-ln u_j).  Words: x -> E_min, y -> argmin, z -> E2, w -> the
+// second member.  The group holding the root token s takes E_min = E_root
+// with s as its argmin.
+struct GroupNoise { float e_min, e2; int arg, arg2; };
+__device__ __forceinline__ GroupNoise group_noise_from(const NoiseRoot& root, U4 w, int n, bool holds_root,
+                                                       int mem_s) {
+  GroupNoise g;
+  if (holds_root) {
+    g.e_min = root.e_root;
+    g.arg = mem_s;
+  } else {
+    g.e_min = __fadd_rn(root.e_root, __fdiv_rn(neglog(uniform_open(w.x)), float(n)));
+    g.arg = int(select_index32(w.y, uint32_t(n)));
+  }
+  if (n >= 2) {
+    g.e2 = __fadd_rn(g.e_min, __fdiv_rn(neglog(uniform_open(w.z)), float(n - 1)));
+    const int i2 = int(select_index32(w.w, uint32_t(n - 1)));
+    g.arg2 = i2 < g.arg ? i2 : i2 + 1;
+  } else {
+    g.e2 = INFINITY;
+    g.arg2 = -1;
+  }
   return g;
 }
-__device__ __forceinline__ GroupMin noise_group(const NoiseKey& k, const NoiseRoot& root,
-                                                int64_t gid, uint32_t ctr, int odd, int n,
-                                                int64_t gid_s, int mem_s) {
-  GroupMin g;
-  if (gid == gid_s) { g.e_min = root.e_root; g.arg = mem_s; return g; }
-  U4 w = philox_at(k, ctr, kTagGroup);
-  return odd ? group_min_from(root, w.z, w.w, n) : group_min_from(root, w.x, w.y, n);
+__device__ __forceinline__ GroupNoise noise_group(const NoiseKey& k, const NoiseRoot& root, int64_t gid, int n,
+                                                  int64_t gid_s, int mem_s) {
+  return group_noise_from(root, philox_at(k, uint32_t(gid), kTagGroup), n, gid == gid_s, mem_s);
 }
-// Noise of token j (global id) that is member `mem` of a group with minimum g.
-__device__ __forceinline__ float noise_token(const NoiseKey& k, const GroupMin& g, int64_t j, int mem) {
+// Noise of token j (global id) that is member `mem` of group g.
+__device__ __forceinline__ float noise_token(const NoiseKey& k, const GroupNoise& g, int64_t j, int mem) {
   if (mem == g.arg) return g.e_min;
+  if (mem == g.arg2) return g.e2;
   U4 w = philox_at(k, uint32_t(j >> 2), kTagToken);
   uint32_t word = (j & 3) == 0 ? w.x : (j & 3) == 1 ? w.y : (j & 3) == 2 ? w.z : w.w;
-  return __fadd_rn(g.e_min, neglog(uniform_open(word)));
+  return __fadd_rn(g.e2, neglog(uniform_open(word)));
 }
 
 // Global group id of token j in a row of V ids, plus its member index.
@@ -221,22 +239,6 @@ __device__ __forceinline__ int64_t slice_group_base(int g, int64_t V) {
   for (int s = 0; s < g; ++s) base += slice_groups(slice_start(s + 1, V) - slice_start(s, V));
   return base;
 }
-// First Philox counter of slice g's group noise (one counter per tile pair
-// and lane).
-__host__ __device__ __forceinline__ int64_t slice_pair_base(int g, int64_t V) {
-  int64_t base = 0;
-  for (int s = 0; s < g; ++s) {
-    int64_t L = slice_start(s + 1, V) - slice_start(s, V);
-    base += (((L + kTile - 1) / kTile + 1) / 2) * kGroupLanes;
-  }
-  return base;
-}
-// Philox counter and word pair of local group lg of a slice.
-__host__ __device__ __forceinline__ uint32_t group_ctr(int64_t pair_base, int64_t lg) {
-  return uint32_t(pair_base + (lg >> 6) * kGroupLanes + (lg & 31));
-}
-__host__ __device__ __forceinline__ int group_odd(int64_t lg) { return int((lg >> 5) & 1); }
-
 // ---------------------------------------------------------------- softmax numerics
 // Canonical arithmetic of the sampler's softmax, shared by every kernel:
 //   c1 = RN(log2(e) / T);  for a slice with max xm: c0 = -RN(xm * c1)

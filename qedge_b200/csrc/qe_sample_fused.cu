@@ -40,8 +40,9 @@ namespace qe {
 namespace fz {
 
 constexpr int kMaxR = 4;          // race candidates tested per row
-constexpr int kMaxItems = 2;      // tile pairs a warp owns per row
+constexpr int kMaxItems = 1;      // tile pairs a warp owns per row
 constexpr int kSlots = 2 * kMaxItems;  // groups per lane
+static_assert(kSlots == 2, "slot selects below assume one tile pair per warp");
 constexpr int kGatherCap = 1024;  // gathered keys per CTA
 constexpr int kSmallK = 64;       // top-k rows up to this k take the gather path
 constexpr uint32_t kWaitLimit = 1u << 26;
@@ -67,9 +68,9 @@ struct alignas(16) Share {
   uint32_t lkey;
   int ngather;
   int overflow;
-  int pad;
+  float ceil;            // bound on the ratio of every token not in cand[]
   Cand cand[kMaxR];
-  unsigned long long sfix;
+  double S;              // softmax sum in this CTA's scale
   long long cnt[kMaxR];
   double F[kMaxR];
 };
@@ -78,14 +79,15 @@ struct RowState {
   int type;
   int out;
   int status;
-  int R;
+  int R;                 // candidates tested this round (gather: keys, -1 = gather pending)
+  int cb;                // first candidate tested this round
+  int ncand;             // candidates known to precede every unpublished token
   int p_on, k_on, k;
   float tp;
   float c1, nM, xM, Sf;
   double S;
   float L;               // gather lower bound (x' >= L)
-  float theta;           // row-scale race threshold from the seeds
-  Cand cand[kMaxR];      // global candidates, race order (approximate)
+  Cand cand[kMaxR];      // global candidates, race order, row-scale ratios
 };
 
 template <int CL>
@@ -115,11 +117,13 @@ struct Misc {
   int s_mem;
   long long s_gid;
   unsigned int wtop[16 * 8];
+  float theta;           // running race threshold of the CTA (positive floats as ints)
+  float wceil[16];
   float wb[16];
   int wbslot[16];
+  double wS[16];
   float wF[16][kMaxR];
   long long wcnt[16][kMaxR];
-  unsigned long long wsfix[16];
   float c0peer[16];
   long long tstart[17];
   long long tgbase[16];
@@ -197,7 +201,7 @@ struct Geo {
   int L[2];
   int ntiles[2], npairs[2];
   int nitems;
-  int64_t gbase[2], pbase[2];  // group id / Philox counter bases of each unit
+  int64_t gbase[2];            // global group id base of each unit
 };
 
 template <int U>
@@ -217,11 +221,10 @@ __device__ __forceinline__ Geo make_geo(int q, int64_t V) {
       g.ntiles[u] = (g.L[u] + kTile - 1) / kTile;
       g.npairs[u] = (g.ntiles[u] + 1) / 2;
       g.gbase[u] = slice_group_base(s, V);
-      g.pbase[u] = slice_pair_base(s, V);
       g.nitems += g.npairs[u];
     } else {
       g.ustart[u] = g.uend[u] = g.cta_end;
-      g.uoff[u] = 0; g.L[u] = 0; g.ntiles[u] = 0; g.npairs[u] = 0; g.gbase[u] = 0; g.pbase[u] = 0;
+      g.uoff[u] = 0; g.L[u] = 0; g.ntiles[u] = 0; g.npairs[u] = 0; g.gbase[u] = 0;
     }
   }
   return g;
@@ -231,7 +234,7 @@ __device__ __forceinline__ void item_of(const Geo& g, int item, int& u, int& p) 
 }
 struct Unit {
   int L, uoff, ntiles;
-  int64_t ustart, uend, gbase, pbase;
+  int64_t ustart, uend, gbase;
 };
 __device__ __forceinline__ Unit unit_of(const Geo& g, int u) {
   Unit r;
@@ -241,7 +244,6 @@ __device__ __forceinline__ Unit unit_of(const Geo& g, int u) {
   r.ustart = u ? g.ustart[1] : g.ustart[0];
   r.uend = u ? g.uend[1] : g.uend[0];
   r.gbase = u ? g.gbase[1] : g.gbase[0];
-  r.pbase = u ? g.pbase[1] : g.pbase[0];
   return r;
 }
 // Warp-aggregated append of the flagged elements (bit i of `mask` flags
@@ -294,8 +296,7 @@ __device__ __forceinline__ float tree_noise(const NoiseKey& key, const NoiseRoot
   while (s + 1 < kNumSlices && slice_start(s + 1, V) <= j) ++s;
   const int64_t a = slice_start(s, V), L = slice_start(s + 1, V) - a;
   const int64_t o = j - a, lg = local_group(o);
-  const GroupMin gm = noise_group(key, root, slice_group_base(s, V) + lg, group_ctr(slice_pair_base(s, V), lg),
-                                  group_odd(lg), group_size(lg, L), gid_s, mem_s);
+  const GroupNoise gm = noise_group(key, root, slice_group_base(s, V) + lg, int(group_size(lg, L)), gid_s, mem_s);
   return noise_token(key, gm, j, member_index(o));
 }
 
@@ -642,7 +643,7 @@ __device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg
 
 // ---------------------------------------------------------------- the kernel
 template <typename T, int CL>
-__global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(FusedParams P) {
+__global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(FusedParams P) {
   constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
   using SM = Smem<T, CL>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -703,7 +704,8 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     const size_t nbytes = size_t(n_cta) * sizeof(T);
     const size_t bulk = P.tma_ok ? (nbytes & ~size_t(15)) : 0;
     if (threadIdx.x == 0) {
-      ms.nan = 0; ms.gmin = 0xFFFFFFFFu; ms.umaxkey[0] = ms.umaxkey[1] = 0u; ms.ngather = 0;
+      ms.nan = 0; ms.gmin = 0xFFFFFFFFu; ms.umaxkey[0] = ms.umaxkey[1] = 0u; ms.ngather = 0; ms.theta = 0.f;
+      for (int w = 0; w < NW; ++w) ms.wb[w] = 0.f;
       if (bulk) {
         fence_proxy_async();
         mbar_expect_tx(&ms.mbar, uint32_t(bulk));
@@ -838,11 +840,16 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     const float c0 = max_coef(cmax, c1);
     const bool race_ok = need_race && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY;
 
-    // greedy: first id holding the CTA max (NaN first if any)
+    // greedy: first id holding the CTA max (NaN first if any).  Needed for
+    // greedy and top-k=1 rows, and for rows that turn out non-finite; only a
+    // CTA whose own maximum is NaN, infinite or overflows can make a row
+    // non-finite, so the scan is skipped everywhere else.
+    const bool need_gidx = greedy || (k_on && kk == 1) || cnan || !(cmax > -INFINITY) ||
+                           cmax == INFINITY || !(fabsf(c0) < INFINITY);
 #pragma unroll
     for (int k = 0; k < kMaxItems; ++k) {
       const int item = warp + k * NW;
-      if (item < geo.nitems) {
+      if (need_gidx && item < geo.nitems) {
         int u, p;
         item_of(geo, item, u, p);
         const Unit un = unit_of(geo, u);
@@ -909,12 +916,22 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     }
 
     // ------------------------------------------------------------ race (local, CTA scale)
-    const int Rr = !(p_on || k_on) ? 1 : ((p_on && !k_on && tp >= 0.99f) ? 2 : kMaxR);
+    // Every CTA finds its own best Rloc tokens exactly.  A group's best ratio
+    // is bounded by max(e_arg / E_min, e_max / E2) (its argmin member against
+    // the group minimum, every other member against the second smallest
+    // value); each warp expands its best-bound group, then every group whose
+    // bound still reaches the CTA's Rloc-th best.  What stays unexpanded is
+    // summarised by a ceiling on the ratio of every unpublished token.
+    // Bounds use approximate logs and divisions (1e-3 margin).
+    const bool filtered = p_on || k_on;
+    const int Rloc = filtered ? 2 : 1;   // tokens a CTA publishes
+    const int Rr = filtered ? 3 : 1;     // per-warp list length (one more for the ceiling)
     float bnd[kSlots];
-    uint32_t uw[kSlots], sw[kSlots];
+    float gn_min[kSlots], gn_e2[kSlots];   // exact group noise of the lane's groups
+    int gn_arg[kSlots];                    // argmin | second member << 8
     unsigned done_mask = 0;
 #pragma unroll
-    for (int s = 0; s < kSlots; ++s) { bnd[s] = -1.f; uw[s] = 0u; sw[s] = 0u; }
+    for (int s = 0; s < kSlots; ++s) { bnd[s] = -1.f; gn_min[s] = 1.f; gn_e2[s] = 1.f; gn_arg[s] = 0; }
     float e_root = 0.f;
     int64_t gid_s = -1;
     int mem_s = 0;
@@ -930,28 +947,33 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           int u, p;
           item_of(geo, item, u, p);
           const Unit un = unit_of(geo, u);
-          U4 w{0, 0, 0, 0};
-          if (!parity) w = philox_at(nkey, uint32_t(un.pbase + p * 32 + lane), kTagGroup);
 #pragma unroll
           for (int tt = 0; tt < 2; ++tt) {
             const int s = 2 * k + tt;
             const int t = 2 * p + tt;
             const int lg = t * 32 + lane;
             const int n = t < un.ntiles ? group_size(lg, un.L) : 0;
-            uw[s] = tt ? w.z : w.x;
-            sw[s] = tt ? w.w : w.y;
             if (n > 0 && gmax[s] > -INFINITY) {
-              float ea;
-              if (parity) ea = gE[s];
-              else if (un.gbase + lg == gid_s) ea = e_root;
-              else ea = e_root + (-0.6931472f * __log2f(uniform_open(uw[s]))) * __frcp_rn(float(n));
-              bnd[s] = __fdividef(unnorm(gmax[s], c1, c0), ea);
+              const float emax = unnorm(gmax[s], c1, c0);
+              if (parity) {
+                bnd[s] = __fdividef(emax, gE[s]);
+              } else {
+                const GroupNoise gn = noise_group(nkey, NoiseRoot{e_root, 0}, un.gbase + lg, n, gid_s, mem_s);
+                gn_min[s] = gn.e_min;
+                gn_e2[s] = gn.e2;
+                gn_arg[s] = gn.arg | ((gn.arg2 & 0xFF) << 8);
+                const float xa = load1<T>(data, pen, use_pen, rpv, un.uoff + int(member_offset(lg, gn.arg)));
+                float b = __fdividef(unnorm(xa, c1, c0), gn.e_min);
+                if (n >= 2) b = fmaxf(b, __fdividef(emax, gn.e2));
+                bnd[s] = b;
+              }
             }
           }
         }
       }
     }
-    // warp-cooperative exact evaluation of slot `s` of lane `ol`
+    // warp-cooperative exact evaluation of slot `s` of lane `ol` (lane m
+    // takes member m)
     auto eval_group = [&](int s, int ol) {
       const int k = s >> 1, tt = s & 1;
       const int item = warp + k * NW;
@@ -960,194 +982,97 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
       const Unit un = unit_of(geo, u);
       const int t = 2 * p + tt;
       const int lg = t * 32 + ol;
-      const int n = group_size(lg, un.L);
-      uint32_t uo = 0, so = 0;
-      float eo = 0.f;
-#pragma unroll
-      for (int sq = 0; sq < kSlots; ++sq) if (sq == s) { uo = uw[sq]; so = sw[sq]; eo = gE[sq]; }
-      uo = __shfl_sync(0xffffffffu, uo, ol);
-      so = __shfl_sync(0xffffffffu, so, ol);
-      eo = __shfl_sync(0xffffffffu, eo, ol);
-      float emin = eo;
-      int arg = -1;
-      if (!parity) {
-        if (un.gbase + lg == gid_s) { emin = e_root; arg = mem_s; }
-        else { const GroupMin gm = group_min_from(NoiseRoot{e_root, 0}, uo, so, n); emin = gm.e_min; arg = gm.arg; }
-      }
       const int local = int(member_offset(lg, lane));
+      // the owner lane's exact group noise
+      GroupNoise gn;
+      gn.e_min = __shfl_sync(0xffffffffu, s ? gn_min[1] : gn_min[0], ol);
+      gn.e2 = __shfl_sync(0xffffffffu, s ? gn_e2[1] : gn_e2[0], ol);
+      const int ga = __shfl_sync(0xffffffffu, s ? gn_arg[1] : gn_arg[0], ol);
+      gn.arg = ga & 0xFF;
+      gn.arg2 = ((ga >> 8) & 0xFF) == 0xFF ? -1 : ((ga >> 8) & 0xFF);
       float r = -INFINITY, x = 0.f, E = 1.f;
       int id = 0x7FFFFFFF;
       if (local < un.L) {
         x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
         id = int(geo.cta_start + un.uoff + local);
-        if (parity) {
-          E = __ldg(a.noise + row * a.noise_ld + id);
-        } else if (lane == arg) {
-          E = emin;
-        } else {
-          const U4 tw = philox_at(nkey, uint32_t(id >> 2), kTagToken);
-          const int sel = id & 3;
-          const uint32_t word = sel == 0 ? tw.x : sel == 1 ? tw.y : sel == 2 ? tw.z : tw.w;
-          E = __fadd_rn(emin, neglog(uniform_open(word)));
-        }
+        E = parity ? __ldg(a.noise + row * a.noise_ld + id) : noise_token(nkey, gn, id, lane);
         r = __fdiv_rn(unnorm(x, c1, c0), E);
         if (r != r) r = -INFINITY;
       }
       warp_merge(wl, Rr, r, x, E, id);
     };
     if (race_ok) {
-      // seed: the CTA's best-bound group, expanded by its warp
-      float bb = -1.f;
-      int bs = 0;
+      // Each warp expands its unexpanded groups in bound order while the
+      // bound reaches the CTA's running Rloc-th best (a shared maximum of the
+      // warps' own Rloc-th bests, which never exceeds the CTA's).
+      volatile float* th_cta = &ms.theta;
+      volatile float* wbest = ms.wb;
+      for (;;) {
+        float theta = fmaxf(*th_cta, wl[Rloc - 1].r);
+        if (Rloc == 2) {
+          // the second largest of the warps' bests also bounds the CTA's 2nd
+          float b1 = 0.f, b2 = 0.f;
+          for (int w = 0; w < NW; ++w) {
+            const float v = wbest[w];
+            if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+          }
+          theta = fmaxf(theta, b2);
+        }
+        float bb = -1.f;
+        int bs = -1;
 #pragma unroll
-      for (int s = 0; s < kSlots; ++s) if (bnd[s] > bb) { bb = bnd[s]; bs = s; }
-      int code = lane * 8 + bs;
-      for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
-        const int oc = __shfl_xor_sync(0xffffffffu, code, o);
-        if (ob > bb || (ob == bb && oc < code)) { bb = ob; code = oc; }
-      }
-      if (lane == 0) { ms.wb[warp] = bb; ms.wbslot[warp] = code; }
-    }
-    __syncthreads();
-    int bw = 0;
-    if (race_ok) {
-      for (int w = 1; w < NW; ++w) if (ms.wb[w] > ms.wb[bw]) bw = w;
-      if (ms.wb[bw] > 0.f && warp == bw) {
-        const int code = ms.wbslot[bw];
+        for (int s = 0; s < kSlots; ++s)
+          if (!((done_mask >> s) & 1u) && bnd[s] > 0.f && bnd[s] >= theta * 0.9999f && bnd[s] > bb) { bb = bnd[s]; bs = s; }
+        int code = bs >= 0 ? lane * 8 + bs : 0x7FFFFFFF;
+        for (int o = 16; o; o >>= 1) {
+          const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
+          const int oc = __shfl_xor_sync(0xffffffffu, code, o);
+          if (ob > bb || (ob == bb && oc < code)) { bb = ob; code = oc; }
+        }
+        if (code == 0x7FFFFFFF) break;
         if (lane == (code >> 3)) done_mask |= 1u << (code & 7);
         eval_group(code & 7, code >> 3);
+        __syncwarp();
+        const float mine = wl[Rloc - 1].r;
+        if (lane == 0 && mine > 0.f) atomicMax(reinterpret_cast<int*>(&ms.theta), __float_as_int(mine));
+        if (lane == 0) wbest[warp] = wl[0].r;
       }
+      float cm = 0.f;
+#pragma unroll
+      for (int s = 0; s < kSlots; ++s) if (!((done_mask >> s) & 1u) && bnd[s] > cm) cm = bnd[s];
+      for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+      if (lane == 0) ms.wceil[warp] = cm;
+    }
+    {
+      // this CTA's softmax sum in its own scale: sum_G fsum(G) 2^(c0 - c0_G)
+      double sp = 0.0;
+      if (!greedy && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY) {
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s)
+          if (fsum[s] > 0.f) sp += double(__fmul_rn(fsum[s], qe_ex2(__fsub_rn(c0, max_coef(gmax[s], c1)))));
+      }
+      for (int o = 16; o; o >>= 1) sp += __shfl_xor_sync(0xffffffffu, sp, o);
+      if (lane == 0) ms.wS[warp] = sp;
     }
     __syncthreads();
 
-    // ------------------------------------------------------------ exchange 1: maxima, greedy, race seeds
+    // ------------------------------------------------------------ exchange 1: maxima, greedy, sum, race candidates
     {
       Share& my = share[ex & 1];
-      if (threadIdx.x == 0) {
-        my.umax[0] = umax[0]; my.umax[1] = umax[1];
-        my.cmax = cnan ? NAN : cmax;
-        my.c0 = c0;
-        my.nan = cnan ? 1 : 0;
-        my.gidx = int(ms.gmin == 0xFFFFFFFFu ? 0x7FFFFFFF : ms.gmin);
-        my.gval = cnan ? NAN : cmax;
-        my.lkey = topk_lkey;
-        int n = 0;
-        if (race_ok)
-          for (int i = 0; i < Rr; ++i) if (wl_all[bw * kMaxR + i].r > -INFINITY) my.cand[n++] = wl_all[bw * kMaxR + i];
-        my.ncand = n;
-      }
-      cluster.sync();
       if (warp == 0) {
-        // lane r reads peer r
-        float pm = -INFINITY, pc0 = 0.f, gv = -INFINITY;
-        int pn = 0, gi = 0x7FFFFFFF, pnc = 0;
-        uint32_t lk = 0u;
-        float sr[kMaxR];
-#pragma unroll
-        for (int i = 0; i < kMaxR; ++i) sr[i] = -INFINITY;
-        if (lane < CL) {
-          const Share* sp = cluster.map_shared_rank(&share[ex & 1], lane);
-          for (int u = 0; u < U; ++u) pm = fmaxf(pm, sp->umax[u]);
-          pc0 = sp->c0; pn = sp->nan; gi = sp->gidx; gv = sp->gval; lk = sp->lkey; pnc = sp->ncand;
-#pragma unroll
-          for (int i = 0; i < kMaxR; ++i) if (i < pnc) sr[i] = sp->cand[i].r;
-          ms.c0peer[lane] = pc0;
-        }
-        const bool anynan = __any_sync(0xffffffffu, pn != 0);
-        float xM = pm;
-        for (int o = 16; o; o >>= 1) xM = fmaxf(xM, __shfl_xor_sync(0xffffffffu, xM, o));
-        for (int o = 16; o; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
-          if (oi != 0x7FFFFFFF && (gi == 0x7FFFFFFF || argmax_better(ov, oi, gv, gi))) { gv = ov; gi = oi; }
-        }
-        lk = __reduce_max_sync(0xffffffffu, lk);
-        const float nM = max_coef(xM, c1);
-        // global race threshold: the Rr-th best seed ratio, in row scale
-        const float sc = lane < CL ? exp2f(nM - pc0) : 0.f;
-#pragma unroll
-        for (int i = 0; i < kMaxR; ++i) sr[i] = sr[i] > -INFINITY ? sr[i] * sc : -INFINITY;
-        float th = 0.f;
-        for (int round = 0; round < Rr; ++round) {
-          float m = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < kMaxR; ++i) m = fmaxf(m, sr[i]);
-          for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (!(m > -INFINITY)) { th = 0.f; break; }
-          th = m;
-          const uint32_t who = __ballot_sync(0xffffffffu, [&] {
-            bool h = false;
-#pragma unroll
-            for (int i = 0; i < kMaxR; ++i) h |= (sr[i] == m);
-            return h;
-          }());
-          if (lane == __ffs(who) - 1) {
-            bool cl = false;
-#pragma unroll
-            for (int i = 0; i < kMaxR; ++i) if (!cl && sr[i] == m) { sr[i] = -INFINITY; cl = true; }
-          }
-        }
-        if (lane == 0) {
-          rs.xM = xM; rs.nM = nM; rs.c1 = c1;
-          rs.p_on = p_on; rs.k_on = k_on; rs.k = kk; rs.tp = tp;
-          rs.L = lk ? key_to_float(lk) : -INFINITY;
-          const bool nonfinite = anynan || !(xM > -INFINITY) || xM == INFINITY || (!greedy && !(fabsf(nM) < INFINITY));
-          rs.status = greedy ? QE_ROW_GREEDY : (nonfinite ? QE_ROW_NONFINITE : 0);
-          rs.out = gi == 0x7FFFFFFF ? 0 : gi;
-          rs.R = 0;
-          rs.theta = th;
-          if (greedy || nonfinite || (k_on && kk == 1)) rs.type = kDone;
-          else if (small_k) rs.type = kGather;
-          else rs.type = kRaceTest;
-        }
-      }
-      ++ex;
-      __syncthreads();
-    }
-    if (rs.type == kDone) {
-      if (q == 0 && threadIdx.x == 0) {
-        a.out_ids[row] = rs.out;
-        if (a.out_status) a.out_status[row] = rs.status;
-      }
-      __syncthreads();
-      continue;
-    }
-
-    if (rs.type == kRaceTest) {
-      // expand every group whose bound can still reach the row threshold
-      // (bounds use approximate logs and divisions: 1e-3 margin)
-      float theta = rs.theta * exp2f(c0 - rs.nM);
-      if (race_ok) {
-        theta = fmaxf(theta, wl[Rr - 1].r);
-        for (;;) {
-          int fs = -1;
-#pragma unroll
-          for (int s = 0; s < kSlots; ++s)
-            if (fs < 0 && !((done_mask >> s) & 1u) && bnd[s] > 0.f && bnd[s] >= theta * 0.999f) fs = s;
-          const uint32_t who = __ballot_sync(0xffffffffu, fs >= 0);
-          if (!who) break;
-          const int ol = __ffs(who) - 1;
-          const int s = __shfl_sync(0xffffffffu, fs, ol);
-          if (lane == ol) done_mask |= 1u << s;
-          eval_group(s, ol);
-          __syncwarp();
-          theta = fmaxf(theta, wl[Rr - 1].r);
-        }
-      }
-      __syncthreads();
-      // ---------------------------------------------------------- exchange 2: candidates
-      Share& my = share[ex & 1];
-      if (warp == 0) {
-        constexpr int PER = (NW * kMaxR + 31) / 32;
+        // the CTA's best Rloc tokens and the ceiling over everything else
+        constexpr int PER = (NW * 3 + 31) / 32;
         Cand c[PER];
 #pragma unroll
         for (int i = 0; i < PER; ++i) {
           const int idx = lane + 32 * i;
-          c[i] = (race_ok && idx < NW * kMaxR) ? wl_all[idx] : Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
+          const int w = idx / 3, j = idx % 3;
+          c[i] = (race_ok && idx < NW * 3 && j < Rr) ? wl_all[w * kMaxR + j] : Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
         }
         int n = 0;
-        for (int round = 0; round < Rr; ++round) {
+        float third = 0.f;
+        const int want = race_ok ? Rr : 0;
+        for (int round = 0; round < want; ++round) {
           int bi = 0;
 #pragma unroll
           for (int i = 1; i < PER; ++i) if (rbetter(c[i].r, c[i].id, c[bi].r, c[bi].id)) bi = i;
@@ -1162,6 +1087,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
             if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; bl = ol; }
           }
           if (!(br > -INFINITY)) break;
+          if (round == Rloc) { third = br; break; }
           if (lane == bl) {
             my.cand[n] = cb;
 #pragma unroll
@@ -1169,35 +1095,65 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           }
           ++n;
         }
-        if (lane == 0) my.ncand = n;
+        if (lane == 0) {
+          float ceil_r = third;
+          double sv = 0.0;
+          for (int w = 0; w < NW; ++w) {
+            if (race_ok) ceil_r = fmaxf(ceil_r, ms.wceil[w] * 1.0001f);
+            sv += ms.wS[w];
+          }
+          my.ncand = n;
+          my.ceil = ceil_r;
+          my.S = sv;
+          my.umax[0] = umax[0]; my.umax[1] = umax[1];
+          my.c0 = c0;
+          my.nan = cnan ? 1 : 0;
+          my.gidx = int(ms.gmin == 0xFFFFFFFFu ? 0x7FFFFFFF : ms.gmin);
+          my.gval = cnan ? NAN : cmax;
+          my.lkey = topk_lkey;
+        }
       }
       cluster.sync();
       if (warp == 0) {
-        // lane r holds peer r's candidates scaled to the row (double)
-        Cand pc[kMaxR];
-        double pr[kMaxR];
-        int pnc = 0;
+        // lane r reads peer r
+        float pm = -INFINITY, pc0 = 0.f, gv = -INFINITY, pceil = 0.f;
+        int pn = 0, gi = 0x7FFFFFFF, pnc = 0;
+        double pS = 0.0;
+        uint32_t lk = 0u;
+        Cand pc[2];
+        pc[0] = pc[1] = Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
         if (lane < CL) {
           const Share* sp = cluster.map_shared_rank(&share[ex & 1], lane);
-          pnc = sp->ncand;
-          const double scl = exp2(double(rs.nM) - double(ms.c0peer[lane]));
-#pragma unroll
-          for (int i = 0; i < kMaxR; ++i) {
-            if (i < pnc) { pc[i] = sp->cand[i]; pr[i] = double(pc[i].r) * scl; } else { pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < kMaxR; ++i) { pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
+          for (int u = 0; u < U; ++u) pm = fmaxf(pm, sp->umax[u]);
+          pc0 = sp->c0; pn = sp->nan; gi = sp->gidx; gv = sp->gval; lk = sp->lkey; pnc = sp->ncand;
+          pS = sp->S; pceil = sp->ceil;
+          if (pnc > 0) pc[0] = sp->cand[0];
+          if (pnc > 1) pc[1] = sp->cand[1];
         }
-        int n = 0;
-        for (int round = 0; round < Rr; ++round) {
-          int bi = 0;
+        const bool anynan = __any_sync(0xffffffffu, pn != 0);
+        float xM = pm;
+        for (int o = 16; o; o >>= 1) xM = fmaxf(xM, __shfl_xor_sync(0xffffffffu, xM, o));
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
+          if (oi != 0x7FFFFFFF && (gi == 0x7FFFFFFF || argmax_better(ov, oi, gv, gi))) { gv = ov; gi = oi; }
+        }
+        lk = __reduce_max_sync(0xffffffffu, lk);
+        const float nM = max_coef(xM, c1);
+        // row scale: a CTA's ratios and sum times 2^(nM - c0_cta)
+        const double sc = (lane < CL && pnc >= 0 && fabsf(pc0) < INFINITY) ? exp2(double(nM) - double(pc0)) : 0.0;
+        double Sv = lane < CL ? pS * sc : 0.0;
+        for (int o = 16; o; o >>= 1) Sv += __shfl_xor_sync(0xffffffffu, Sv, o);
+        double phi = double(pceil) * sc;
+        for (int o = 16; o; o >>= 1) phi = fmax(phi, __shfl_xor_sync(0xffffffffu, phi, o));
+        double pr[2];
 #pragma unroll
-          for (int i = 1; i < kMaxR; ++i)
-            if (pr[i] > pr[bi] || (pr[i] == pr[bi] && pc[i].id < pc[bi].id)) bi = i;
-          double bv = -1.0; int bid = 0x7FFFFFFF;
-#pragma unroll
-          for (int i = 0; i < kMaxR; ++i) if (i == bi) { bv = pr[i]; bid = pc[i].id; }
+        for (int i = 0; i < 2; ++i) pr[i] = pc[i].r > -INFINITY ? double(pc[i].r) * sc : -1.0;
+        int n = 0, ncomplete = 0;
+        for (int round = 0; round < kMaxR; ++round) {
+          const int bi = (pr[1] > pr[0] || (pr[1] == pr[0] && pc[1].id < pc[0].id)) ? 1 : 0;
+          double bv = bi ? pr[1] : pr[0];
+          int bid = bi ? pc[1].id : pc[0].id;
           int bl = lane;
           for (int o = 16; o; o >>= 1) {
             const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -1207,119 +1163,127 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           }
           if (!(bv >= 0.0) || bid == 0x7FFFFFFF) break;
           if (lane == bl) {
-#pragma unroll
-            for (int i = 0; i < kMaxR; ++i) if (i == bi) { rs.cand[n] = pc[i]; pr[i] = -1.0; pc[i].id = 0x7FFFFFFF; }
+            Cand cb = bi ? pc[1] : pc[0];
+            cb.r = float(bv);
+            rs.cand[n] = cb;
+            if (bi) { pr[1] = -1.0; pc[1].id = 0x7FFFFFFF; } else { pr[0] = -1.0; pc[0].id = 0x7FFFFFFF; }
           }
           ++n;
+          if (bv > phi) ncomplete = n;   // no unpublished token can beat it
         }
+        __syncwarp();
         if (lane == 0) {
-          rs.R = n;
-          if (n == 0) {
+          rs.xM = xM; rs.nM = nM; rs.c1 = c1;
+          rs.p_on = p_on; rs.k_on = k_on; rs.k = kk; rs.tp = tp;
+          rs.L = lk ? key_to_float(lk) : -INFINITY;
+          rs.S = Sv;
+          rs.Sf = float(Sv);
+          const bool nonfinite = anynan || !(xM > -INFINITY) || xM == INFINITY ||
+                                 (!greedy && !(fabsf(nM) < INFINITY));
+          rs.status = greedy ? QE_ROW_GREEDY : (nonfinite ? QE_ROW_NONFINITE : 0);
+          rs.out = gi == 0x7FFFFFFF ? 0 : gi;
+          rs.ncand = ncomplete > 0 ? ncomplete : (n > 0 ? 1 : 0);
+          rs.cb = 0;
+          rs.R = 1;
+          if (greedy || nonfinite || (k_on && kk == 1)) {
+            rs.type = kDone;
+          } else if (small_k) {
+            rs.type = kGather;
+            rs.R = -1;
+          } else if (n == 0 || !(rs.Sf > 0.f) || rs.Sf == INFINITY) {
             rs.type = kDone;
             rs.status = QE_ROW_NONFINITE;
-          } else if (!p_on && !k_on) {
+          } else if (!filtered) {
             rs.type = kDone;
+            rs.out = rs.cand[0].id;
+          } else {
+            rs.type = kRaceTest;
+            rs.L = -INFINITY;
           }
         }
       }
       ++ex;
       __syncthreads();
-      if (rs.type == kDone) {
-        if (q == 0 && threadIdx.x == 0) {
-          a.out_ids[row] = rs.R > 0 ? rs.cand[0].id : rs.out;
-          if (a.out_status) a.out_status[row] = rs.status;
-        }
-        __syncthreads();
-        continue;
+    }
+    if (rs.type == kDone) {
+      if (q == 0 && threadIdx.x == 0) {
+        a.out_ids[row] = rs.out;
+        if (a.out_status) a.out_status[row] = rs.status;
       }
+      __syncthreads();
+      continue;
     }
 
-    // ------------------------------------------------------------ S partial and pass 2 (sparse)
+    // ------------------------------------------------------------ pass 2 (sparse): candidate tests, gather
+    // Round 0 tests the row's best candidate alone (it is in the kept set for
+    // most rows, and its high logit lets most groups be skipped); if it is
+    // rejected, round 1 tests the remaining complete candidates; if those
+    // are rejected too, a gather round collects every token >= the best
+    // rejected candidate (the kept set is a prefix of the order).
     const float nM = rs.nM;
-    const int R = rs.type == kRaceTest ? rs.R : 0;
-    unsigned long long sfl = 0ull;
-#pragma unroll
-    for (int s = 0; s < kSlots; ++s) {
-      if (fsum[s] > 0.f) {
-        const float sc = qe_ex2(__fsub_rn(nM, max_coef(gmax[s], c1)));
-        sfl += __double2ull_rn(double(__fmul_rn(fsum[s], sc)) * kSumScale);
-      }
-    }
-    float cv[kMaxR];
-    int cidv[kMaxR];
-#pragma unroll
-    for (int c = 0; c < kMaxR; ++c) { cv[c] = c < R ? rs.cand[c].x : INFINITY; cidv[c] = c < R ? rs.cand[c].id : 0; }
     float Fl[kMaxR];
-    long long Cl[kMaxR];
+    int Cl[kMaxR];
+#pragma unroll 1
+    for (int round = 0; round < 3; ++round) {
+      const bool do_test = rs.type == kRaceTest;
+      const bool do_gather = rs.type == kGather;
+      const int cb = do_test ? rs.cb : 0;
+      const int R = do_test ? rs.R : 0;
+      float cv[kMaxR];
+      int cidv[kMaxR];
 #pragma unroll
-    for (int c = 0; c < kMaxR; ++c) { Fl[c] = 0.f; Cl[c] = 0; }
-    const bool gather_row = rs.type == kGather;
-    float Lg = rs.L;
-    // two rounds at most: the candidate tests, then (if every candidate was
-    // rejected) a gather of the tokens >= the best rejected candidate
-    for (int round = 0; round < 2; ++round) {
-      const bool do_gather = round == 1 || gather_row;
-      if (round == 1) {
-        if (threadIdx.x == 0) ms.ngather = 0;
-        __syncthreads();
-        Lg = rs.L;
+      for (int c = 0; c < kMaxR; ++c) {
+        cv[c] = c < R ? rs.cand[cb + c].x : INFINITY;
+        cidv[c] = c < R ? rs.cand[cb + c].id : 0;
+        Fl[c] = 0.f;
+        Cl[c] = 0;
       }
+      float thmin = INFINITY;  // tokens at or below this are behind every candidate
 #pragma unroll
-      for (int k = 0; k < kMaxItems; ++k) {
-        const int item = warp + k * NW;
-        if (item < geo.nitems) {
-          int u, p;
-          item_of(geo, item, u, p);
-          const Unit un = unit_of(geo, u);
-          // thresholds: a token is ahead of candidate c iff x > th[c]
-          // (>= v for ids below c's, > v above it; c's own slice is mixed)
-          float th[kMaxR];
-          bool mixed[kMaxR];
+      for (int c = 0; c < kMaxR; ++c) if (c < R) thmin = fminf(thmin, cv[c]);
+      thmin = nextafterf(thmin, -INFINITY);
+      const float Lg = rs.L;
+      if (threadIdx.x == 0) ms.ngather = 0;
+      __syncthreads();
+      const int item = warp;
+      if (item < geo.nitems) {
+        int u, p;
+        item_of(geo, item, u, p);
+        const Unit un = unit_of(geo, u);
+#pragma unroll 1
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * p + tt;
+          const float gm = tt ? gmax[1] : gmax[0];
+          const bool q_test = do_test && t < un.ntiles && gm > thmin;
+          const bool q_gath = do_gather && t < un.ntiles && gm >= Lg;
+          if (__any_sync(0xffffffffu, q_test || q_gath)) {
+#pragma unroll 1
+            for (int b = 0; b < 4; ++b) {
+              const int local = t * kTile + b * 256 + lane * 8;
+              const int nv = max(0, min(8, un.L - local));
+              const int off = un.uoff + local;
+              float x[8];
+              Load8<T>::run(data, off, nv, x);
+              if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
+              if (q_test) {
+                const int id0 = int(geo.cta_start) + off;
 #pragma unroll
-          for (int c = 0; c < kMaxR; ++c) {
-            mixed[c] = c < R && cidv[c] >= un.ustart && cidv[c] < un.uend;
-            th[c] = (c < R && cidv[c] >= un.uend) ? nextafterf(cv[c], -INFINITY) : cv[c];
-          }
-          float thmin = INFINITY;
+                for (int i = 0; i < 8; ++i) {
+                  if (x[i] > thmin) {
+                    // a token is ahead of candidate c iff (x, -id) > (x_c, -id_c)
+                    const float e = unnorm(x[i], c1, nM);
 #pragma unroll
-          for (int c = 0; c < kMaxR; ++c) if (c < R) thmin = fminf(thmin, mixed[c] ? nextafterf(cv[c], -INFINITY) : th[c]);
-#pragma unroll
-          for (int tt = 0; tt < 2; ++tt) {
-            const int s = 2 * k + tt;
-            const int t = 2 * p + tt;
-            const bool q_test = !do_gather && t < un.ntiles && gmax[s] > thmin;
-            const bool q_gath = do_gather && t < un.ntiles && gmax[s] >= Lg;
-            if (__any_sync(0xffffffffu, q_test || q_gath)) {
-#pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const int local = t * kTile + b * 256 + lane * 8;
-                const int nv = max(0, min(8, un.L - local));
-                const int off = un.uoff + local;
-                float x[8];
-                Load8<T>::run(data, off, nv, x);
-                if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
-                if (q_test) {
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) {
-                    if (x[i] > thmin) {
-                      const float e = unnorm(x[i], c1, nM);
-#pragma unroll
-                      for (int c = 0; c < kMaxR; ++c) {
-                        if (c < R) {
-                          bool pred = x[i] > th[c];
-                          if (mixed[c]) pred = pred || (x[i] == cv[c] && int(geo.cta_start + off + i) < cidv[c]);
-                          if (pred) { Fl[c] += e; Cl[c] += 1; }
-                        }
-                      }
+                    for (int c = 0; c < kMaxR; ++c) {
+                      if (c < R && (x[i] > cv[c] || (x[i] == cv[c] && id0 + i < cidv[c]))) { Fl[c] += e; Cl[c] += 1; }
                     }
                   }
                 }
-                if (do_gather) {
-                  unsigned mask = 0;
+              }
+              if (do_gather) {
+                unsigned mask = 0;
 #pragma unroll
-                  for (int i = 0; i < 8; ++i) mask |= ((q_gath && i < nv && x[i] >= Lg) ? 1u : 0u) << i;
-                  gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
-                }
+                for (int i = 0; i < 8; ++i) mask |= ((q_gath && i < nv && x[i] >= Lg) ? 1u : 0u) << i;
+                gather_append(mask, x, geo.cta_start + off, gath, &ms.ngather);
               }
             }
           }
@@ -1328,9 +1292,9 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
       // reductions and exchange
 #pragma unroll
       for (int c = 0; c < kMaxR; ++c) {
-        if (c < R && round == 0) {
+        if (c < R) {
           float f = Fl[c];
-          long long n = Cl[c];
+          int n = Cl[c];
           for (int o = 16; o; o >>= 1) {
             f += __shfl_xor_sync(0xffffffffu, f, o);
             n += __shfl_xor_sync(0xffffffffu, n, o);
@@ -1338,101 +1302,78 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           if (lane == 0) { ms.wF[warp][c] = f; ms.wcnt[warp][c] = n; }
         }
       }
-      if (round == 0) {
-        unsigned long long sv = sfl;
-        for (int o = 16; o; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
-        if (lane == 0) ms.wsfix[warp] = sv;
-      }
       __syncthreads();
       Share& my2 = share[ex & 1];
       if (threadIdx.x == 0) {
-        if (round == 0) {
-          unsigned long long sv = 0;
-          for (int w = 0; w < NW; ++w) sv += ms.wsfix[w];
-          my2.sfix = sv;
-          for (int c = 0; c < R; ++c) {
-            double f = 0.0; long long n = 0;
-            for (int w = 0; w < NW; ++w) { f += double(ms.wF[w][c]); n += ms.wcnt[w][c]; }
-            my2.F[c] = f; my2.cnt[c] = n;
-          }
+        for (int c = 0; c < R; ++c) {
+          double f = 0.0; long long n = 0;
+          for (int w = 0; w < NW; ++w) { f += double(ms.wF[w][c]); n += ms.wcnt[w][c]; }
+          my2.F[c] = f; my2.cnt[c] = n;
         }
         my2.ngather = ms.ngather;
         my2.overflow = ms.ngather > kGatherCap ? 1 : 0;
       }
       cluster.sync();
       if (threadIdx.x < CL) {
-        const Share* s = cluster.map_shared_rank(&share[ex & 1], int(threadIdx.x));
+        const Share* sh = cluster.map_shared_rank(&share[ex & 1], int(threadIdx.x));
         Share& d = peers[threadIdx.x];
-        d.ngather = s->ngather;
-        d.overflow = s->overflow;
-        if (round == 0) {
-          d.sfix = s->sfix;
-          for (int c = 0; c < R; ++c) { d.F[c] = s->F[c]; d.cnt[c] = s->cnt[c]; }
-        }
+        d.ngather = sh->ngather;
+        d.overflow = sh->overflow;
+        for (int c = 0; c < R; ++c) { d.F[c] = sh->F[c]; d.cnt[c] = sh->cnt[c]; }
       }
       __syncthreads();
       if (threadIdx.x == 0) {
         int ngat = 0, ovf = 0;
         for (int r = 0; r < CL; ++r) { ngat += peers[r].ngather; ovf |= peers[r].overflow; }
-        if (round == 0) {
-          unsigned long long sv = 0;
+        if (do_test) {
           double F[kMaxR];
           long long C[kMaxR];
           for (int c = 0; c < kMaxR; ++c) { F[c] = 0.0; C[c] = 0; }
-          for (int r = 0; r < CL; ++r) {
-            sv += peers[r].sfix;
+          for (int r = 0; r < CL; ++r)
             for (int c = 0; c < R; ++c) { F[c] += peers[r].F[c]; C[c] += peers[r].cnt[c]; }
+          // exact ratios; the first candidate in race order inside the kept set wins
+          float rM[kMaxR];
+          int order[kMaxR];
+          for (int c = 0; c < R; ++c) {
+            rM[c] = __fdiv_rn(__fdiv_rn(unnorm(rs.cand[cb + c].x, c1, nM), rs.Sf), rs.cand[cb + c].E);
+            order[c] = c;
           }
-          const double Sd = double(sv) * (1.0 / kSumScale);
-          rs.S = Sd;
-          rs.Sf = float(Sd);
-          if (!(rs.Sf > 0.f) || rs.Sf == INFINITY) {
+          for (int i = 1; i < R; ++i) {
+            const int v = order[i];
+            int j = i;
+            while (j > 0 && rbetter(rM[v], rs.cand[cb + v].id, rM[order[j - 1]], rs.cand[cb + order[j - 1]].id)) {
+              order[j] = order[j - 1]; --j;
+            }
+            order[j] = v;
+          }
+          int win = -1;
+          float Lx = rs.L;
+          for (int i = 0; i < R; ++i) {
+            const int c = order[i];
+            const bool okp = !p_on || F[c] <= double(tp) * rs.S;
+            const bool okk = !k_on || C[c] < kk;
+            if (okp && okk) { win = c; break; }
+            Lx = fmaxf(Lx, rs.cand[cb + c].x);
+          }
+          rs.L = Lx;
+          if (win >= 0) {
             rs.type = kDone;
-            rs.status = QE_ROW_NONFINITE;
-          } else if (rs.type == kRaceTest) {
-            // exact ratios; the first candidate in race order inside the kept set wins
-            float rM[kMaxR];
-            int order[kMaxR];
-            for (int c = 0; c < R; ++c) {
-              rM[c] = __fdiv_rn(__fdiv_rn(unnorm(rs.cand[c].x, c1, nM), rs.Sf), rs.cand[c].E);
-              order[c] = c;
-            }
-            for (int i = 1; i < R; ++i) {
-              const int v = order[i];
-              int j = i;
-              while (j > 0 && rbetter(rM[v], rs.cand[v].id, rM[order[j - 1]], rs.cand[order[j - 1]].id)) {
-                order[j] = order[j - 1]; --j;
-              }
-              order[j] = v;
-            }
-            int win = -1;
-            float Lx = -INFINITY;
-            for (int i = 0; i < R; ++i) {
-              const int c = order[i];
-              const bool okp = !p_on || F[c] <= double(tp) * Sd;
-              const bool okk = !k_on || C[c] < kk;
-              if (okp && okk) { win = c; break; }
-              Lx = fmaxf(Lx, rs.cand[c].x);
-            }
-            if (win >= 0) {
-              rs.type = kDone;
-              rs.out = rs.cand[win].id;
-            } else {
-              rs.type = kGather;  // every kept token is >= the best rejected candidate
-              rs.L = Lx;
-            }
-          } else if (ovf || ngat > P.merge_cap) {
-            rs.type = kSlow;
+            rs.out = rs.cand[cb + win].id;
+          } else if (cb + R < rs.ncand) {
+            rs.cb = cb + R;                       // test the remaining complete candidates
+            rs.R = rs.ncand - (cb + R);
+          } else {
+            rs.type = kGather;                    // every kept token is >= the best rejected candidate
+            rs.R = -1;
           }
-        } else if (ovf || ngat > P.merge_cap) {
-          rs.type = kSlow;
+        } else {
+          rs.type = (ovf || ngat > P.merge_cap) ? kSlow : kGather;
+          rs.R = ngat;
         }
-        rs.R = rs.type == kGather ? ngat : rs.R;
-        if (round == 0 && rs.type == kGather && !gather_row) rs.R = -1;  // needs the gather round
       }
       ++ex;
       __syncthreads();
-      if (!(rs.type == kGather && rs.R == -1)) break;
+      if (!(rs.type == kRaceTest || (rs.type == kGather && rs.R == -1))) break;
     }
     if (rs.type == kDone) {
       if (q == 0 && threadIdx.x == 0) {

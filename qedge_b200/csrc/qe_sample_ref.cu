@@ -402,7 +402,6 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
     token_group(root.s, V, &gid_s, &mem_s);
   }
   const int64_t gbase = slice_group_base(g, V);
-  const int64_t pbase = slice_pair_base(g, V);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float rb = -INFINITY; int64_t ib = INT64_MAX;
   for (int64_t c0 = s0; c0 < s1; c0 += blockDim.x) {
@@ -435,9 +434,7 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
         const int64_t o = j - s0;
         const int64_t gid = gbase + local_group(o);
         const int mem = member_index(o);
-        const int64_t lg = local_group(o);
-        const GroupMin gm = noise_group(key, root, gid, group_ctr(pbase, lg), group_odd(lg),
-                                        group_size(lg, L), gid_s, mem_s);
+        const GroupNoise gm = noise_group(key, root, gid, group_size(local_group(o), L), gid_s, mem_s);
         E = noise_token(key, gm, j, mem);
       }
       const float r = __fdiv_rn(p, E);

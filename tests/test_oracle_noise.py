@@ -35,16 +35,37 @@ def test_neglog_accuracy():
 
 def test_group_layout_partitions_vocab():
     for V in (1, 7, 8, 1000, 1024, 4099, 248_320):
-        gid, mem, sizes, ctrs = N.group_layout(V)
+        gid, mem, sizes = N.group_layout(V)
         assert sizes.sum() == V
         assert np.all(np.bincount(gid, minlength=sizes.size) == sizes)
         # members are numbered 0..n-1 in increasing id order inside each group
         order = np.lexsort((np.arange(V), gid))
         ranks = np.arange(V) - np.searchsorted(gid[order], gid[order])
         assert np.all(mem[order] == ranks)
-        # every (Philox counter, word pair) is used by exactly one group
-        keys = ctrs[:, 0] * 2 + ctrs[:, 1]
-        assert np.unique(keys).size == keys.size
+
+
+def test_group_order_statistics():
+    """Inside every group the noise is minimum-first: one member holds the
+    group minimum, one the second smallest value, and the gap between them
+    is Exp(1)/(n-1); the second member is uniform among the others."""
+    V = 248_320
+    E = N.philox_noise(2, V, seed=77, step=3)
+    gid, mem, sizes = N.group_layout(V)
+    full = sizes[gid] == 32
+    gaps, pos2 = [], []
+    for r in range(2):
+        e = E[r][full]
+        g = gid[full]
+        order = np.lexsort((e, g))
+        eg, gg, mg = e[order], g[order], mem[full][order]
+        first = np.r_[True, gg[1:] != gg[:-1]]
+        idx = np.flatnonzero(first)
+        gaps.append((eg[idx + 1] - eg[idx]) * 31.0)
+        pos2.append(mg[idx + 1])
+    gaps = np.concatenate(gaps)
+    assert stats.kstest(gaps, "expon").pvalue > 1e-3
+    counts = np.bincount(np.concatenate(pos2), minlength=32)
+    assert stats.chisquare(counts).pvalue > 1e-3
 
 
 def test_philox_noise_is_exp1():
