@@ -113,6 +113,38 @@ const char* qe_last_error(void);
  * writes the scratch it reads first.  Allocates nothing. */
 int qe_sample_noalloc(const qe_sample_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Vocab-sharded sampling (tensor-parallel lm_head).  The reference samples
+ * one full [B, V] logits tensor (src/compute/sampler.py:25-41); these calls
+ * let each of `nshards` GPUs (1, 2, 4, 8 or 16) keep its own contiguous
+ * block of the vocabulary: shard s holds canonical slices
+ * [s*16/nshards, (s+1)*16/nshards), i.e. ids
+ * [floor(s*V/(8*nshards))*8, floor((s+1)*V/(8*nshards))*8).  In every call
+ * `args->vocab` is the full V, `args->logits` (and `noise`) point at the
+ * shard's first column with row stride `ld` (`noise_ld`), and the other
+ * fields mean what they mean for qe_sample (`workspace` is unused).  V must be
+ * <= 262,144.  A step:
+ *   1. qe_shard_summarize   -> records [B][16/nshards] on every GPU
+ *   2. all-gather records   -> [nshards][B][16/nshards] (e.g. NCCL)
+ *   3. qe_shard_merge       -> out_ids for every row that needs no test;
+ *                              tests [B] for the rest (identical on every GPU)
+ *   4. qe_shard_test        -> partials [B][16/nshards]
+ *   5. all-gather partials  -> [nshards][B][16/nshards]
+ *   6. qe_shard_decide      -> the remaining out_ids.  A row whose candidates
+ *      all fall outside its kept set gets id -1 and status QE_ROW_SLOW; the
+ *      caller finishes it exactly (gather that row, call qe_sample).
+ * Greedy, small top-k (<= 64) and unfiltered rows are final after step 3.
+ * Token ids equal the single-GPU ones under the same noise. */
+size_t qe_shard_record_bytes(void);   /* bytes per (row, slice) record */
+size_t qe_shard_test_bytes(void);     /* bytes per row of `tests` */
+size_t qe_shard_partial_bytes(void);  /* bytes per (row, slice) partial */
+int qe_shard_summarize(const qe_sample_args* args, int shard, int nshards, void* records, void* stream);
+int qe_shard_merge(const qe_sample_args* args, int nshards, const void* all_records, void* tests, void* stream);
+int qe_shard_test(const qe_sample_args* args, int shard, int nshards, const void* tests, void* partials,
+                  void* stream);
+int qe_shard_decide(const qe_sample_args* args, int nshards, const void* tests, const void* all_partials,
+                    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,7 +20,8 @@ STATUS_NAMES = {0: "QE_OK", -1: "QE_ERR_INVALID", -2: "QE_ERR_CUDA",
 
 # Every symbol the header declares; tests check the library exports them.
 EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error",
-            "qe_sample_noalloc")
+            "qe_sample_noalloc", "qe_shard_record_bytes", "qe_shard_test_bytes", "qe_shard_partial_bytes",
+            "qe_shard_summarize", "qe_shard_merge", "qe_shard_test", "qe_shard_decide")
 QE_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _vp = ctypes.c_void_p
@@ -85,6 +86,18 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
         lib.qe_sample_noalloc.argtypes = [ctypes.POINTER(QeSampleArgs), _vp]
         lib.qe_last_error.restype = ctypes.c_char_p
         lib.qe_last_error.argtypes = []
+        for name in ("qe_shard_record_bytes", "qe_shard_test_bytes", "qe_shard_partial_bytes"):
+            getattr(lib, name).restype = ctypes.c_size_t
+            getattr(lib, name).argtypes = []
+        _a = ctypes.POINTER(QeSampleArgs)
+        lib.qe_shard_summarize.restype = ctypes.c_int
+        lib.qe_shard_summarize.argtypes = [_a, ctypes.c_int, ctypes.c_int, _vp, _vp]
+        lib.qe_shard_merge.restype = ctypes.c_int
+        lib.qe_shard_merge.argtypes = [_a, ctypes.c_int, _vp, _vp, _vp]
+        lib.qe_shard_test.restype = ctypes.c_int
+        lib.qe_shard_test.argtypes = [_a, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
+        lib.qe_shard_decide.restype = ctypes.c_int
+        lib.qe_shard_decide.argtypes = [_a, ctypes.c_int, _vp, _vp, _vp]
         ver = lib.qe_abi_version()
         if ver != QE_ABI_VERSION:
             raise NativeError(f"libqesample ABI {ver} != expected {QE_ABI_VERSION}")

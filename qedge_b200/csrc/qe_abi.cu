@@ -115,7 +115,12 @@ extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
   // debug probabilities are requested, or the vocabulary is too large
   const char* env = std::getenv("QE_SAMPLER_PATH");
   const int forced = (env && !std::strcmp(env, "ref")) ? 1 : (env && !std::strcmp(env, "fused")) ? 2 : 0;
-  const int cluster = a->dtype == QE_DTYPE_F32 ? 8 : 16;
+  // 8 CTAs x 512 threads per row (measured faster than 16 x 256 on B200 for
+  // every dtype); QE_FUSED_CLUSTER=16 selects the 16-CTA shape for 16-bit rows
+  int cluster = 8;
+  if (const char* cl = std::getenv("QE_FUSED_CLUSTER")) {
+    if (cl[0] == '1' && cl[1] == '6' && a->dtype != QE_DTYPE_F32) cluster = 16;
+  }
   const bool fused_ok = !a->out_probs && fused_capacity(a->vocab, cluster) > 0;
   if (forced != 1 && fused_ok) return launch_fused(ka, st, cluster);
   if (forced == 2 && !fused_ok && !a->out_probs) return set_error(QE_ERR_UNSUPPORTED, "QE_SAMPLER_PATH=fused but the fused path cannot take this call");

@@ -239,6 +239,17 @@ __device__ __forceinline__ int64_t slice_group_base(int g, int64_t V) {
   for (int s = 0; s < g; ++s) base += slice_groups(slice_start(s + 1, V) - slice_start(s, V));
   return base;
 }
+// Noise of global token j under the Philox tree (any CTA can evaluate it).
+__device__ __forceinline__ float tree_noise(const NoiseKey& key, const NoiseRoot& root, int64_t gid_s,
+                                            int mem_s, int64_t j, int64_t V) {
+  int s = 0;
+  while (s + 1 < kNumSlices && slice_start(s + 1, V) <= j) ++s;
+  const int64_t a = slice_start(s, V), L = slice_start(s + 1, V) - a;
+  const int64_t o = j - a, lg = local_group(o);
+  const GroupNoise gm = noise_group(key, root, slice_group_base(s, V) + lg, int(group_size(lg, L)), gid_s, mem_s);
+  return noise_token(key, gm, j, member_index(o));
+}
+
 // ---------------------------------------------------------------- softmax numerics
 // Canonical arithmetic of the sampler's softmax, shared by every kernel:
 //   c1 = RN(log2(e) / T);  for a slice with max xm: c0 = -RN(xm * c1)
@@ -253,6 +264,16 @@ __device__ __forceinline__ float qe_ex2(float a) {
   asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(a));
   return r;
 }
+// Flush-to-zero variant (one SFU instruction).  Identical to qe_ex2 except
+// that results below 2^-126 become 0; the fused path uses it everywhere: such
+// terms are below half an ulp of every sum they enter (each sum holds a term
+// of 1) and a token with e < 2^-126 can never win the race.
+__device__ __forceinline__ float qe_ex2_ftz(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ float unnorm_ftz(float x, float c1, float c0) { return qe_ex2_ftz(__fmaf_rn(x, c1, c0)); }
 __device__ __forceinline__ float temp_coef(float T) { return __fdiv_rn(1.4426950408889634f, T); }
 __device__ __forceinline__ float max_coef(float xm, float c1) { return -__fmul_rn(xm, c1); }
 __device__ __forceinline__ float unnorm(float x, float c1, float c0) { return qe_ex2(__fmaf_rn(x, c1, c0)); }

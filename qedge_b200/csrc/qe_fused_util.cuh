@@ -25,13 +25,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 // Bounded wait on an mbarrier phase.  Returns false if the phase did not
 // complete within `limit` polls (the caller records an error; it never hangs).
+// Each poll may suspend the thread for up to kTryWaitHintNs (it resumes as
+// soon as the phase completes), so the bound is limit * kTryWaitHintNs.
+constexpr uint32_t kTryWaitHintNs = 1000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
   uint32_t done = 0;
   for (uint32_t i = 0; i < limit; ++i) {
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitHintNs)
         : "memory");
     if (done) return true;
   }

@@ -43,9 +43,9 @@ constexpr int kMaxR = 4;          // race candidates tested per row
 constexpr int kMaxItems = 1;      // tile pairs a warp owns per row
 constexpr int kSlots = 2 * kMaxItems;  // groups per lane
 static_assert(kSlots == 2, "slot selects below assume one tile pair per warp");
-constexpr int kGatherCap = 1024;  // gathered keys per CTA
+constexpr int kGatherCap = 768;   // gathered keys per CTA
 constexpr int kSmallK = 64;       // top-k rows up to this k take the gather path
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint32_t kWaitLimit = 1u << 20;   // polls (each suspends up to 1 us)
 
 enum RowType : int { kDone = 0, kRaceTest = 1, kGather = 2, kSlow = 3 };
 
@@ -56,24 +56,32 @@ struct Cand {
   int id;    // token id
 };
 
-// What a CTA publishes to its cluster peers (read over DSMEM).
+// What a CTA publishes to its cluster peers in the candidate-test and gather
+// rounds (read over DSMEM).
 struct alignas(16) Share {
-  float umax[2];
-  float cmax;
-  float c0;
-  int nan;
-  int ncand;
-  int gidx;
-  float gval;
-  uint32_t lkey;
   int ngather;
   int overflow;
-  float ceil;            // bound on the ratio of every token not in cand[]
-  Cand cand[kMaxR];
-  double S;              // softmax sum in this CTA's scale
+  int pad[2];
   long long cnt[kMaxR];
   double F[kMaxR];
 };
+
+// Exchange-1 record: what a CTA pushes into every peer's inbox (DSMEM
+// stores before the cluster barrier; each CTA then reads its own inbox).
+struct alignas(16) Rec1 {
+  float umax[2];
+  float c0;
+  int nan;
+  int gidx;
+  float gval;
+  uint32_t lkey;
+  int ncand;
+  float ceil;            // bound on the ratio of every token not in cand[]
+  int pad;
+  double S;              // softmax sum in this CTA's scale
+  Cand cand[2];
+};
+static_assert(sizeof(Rec1) % 16 == 0, "Rec1 is copied as 16-byte words");
 
 struct RowState {
   int type;
@@ -130,6 +138,13 @@ struct Misc {
   int slow_int[48];
 };
 
+// Exact noise of one group, kept in shared memory between the noise pass and
+// the expansions (parity mode: e_min is the group's minimum noise).
+struct GNoise {
+  float e_min, e2;
+  int args;  // argmin | second member << 8 (0xFF: none)
+};
+
 // ---------------------------------------------------------------- smem layout
 template <typename T, int CL>
 struct Smem {
@@ -142,7 +157,11 @@ struct Smem {
   static __host__ __device__ size_t wl_off(int cap) { return peer_off(cap) + size_t(CL) * sizeof(Share); }
   static __host__ __device__ size_t rs_off(int cap) { return wl_off(cap) + size_t(NW) * kMaxR * sizeof(Cand); }
   static __host__ __device__ size_t misc_off(int cap) { return (rs_off(cap) + sizeof(RowState) + 15) / 16 * 16; }
-  static __host__ __device__ size_t total(int cap) { return misc_off(cap) + (sizeof(Misc) + 127) / 128 * 128; }
+  static __host__ __device__ size_t gnz_off(int cap) { return misc_off(cap) + (sizeof(Misc) + 127) / 128 * 128; }
+  static __host__ __device__ size_t inbox_off(int cap) {
+    return (gnz_off(cap) + size_t(Cfg<CL>::NT) * kSlots * sizeof(GNoise) + 15) / 16 * 16;
+  }
+  static __host__ __device__ size_t total(int cap) { return inbox_off(cap) + 2 * size_t(CL) * sizeof(Rec1); }
 };
 
 // ---------------------------------------------------------------- small helpers
@@ -191,6 +210,16 @@ __device__ __forceinline__ void warp_merge(Cand* wl, int n, float r, float x, fl
     if (stop) break;
     if (lane == bl) key = 0ull;
   }
+}
+
+// Lane holding the warp-wide best (r desc, id asc) among the lanes' (r, id),
+// or -1 if no lane has r > -inf.  Two warp reductions and a ballot.
+__device__ __forceinline__ int warp_best_lane(float r, int id) {
+  const uint32_t k = (r > -INFINITY) ? ordered_key(r) : 0u;   // NaN never reaches here
+  const uint32_t km = __reduce_max_sync(0xffffffffu, k);
+  if (km == 0u) return -1;
+  const uint32_t im = __reduce_min_sync(0xffffffffu, k == km ? uint32_t(id) : 0xFFFFFFFFu);
+  return __ffs(__ballot_sync(0xffffffffu, k == km && uint32_t(id) == im)) - 1;
 }
 
 // ---------------------------------------------------------------- per-row geometry
@@ -289,16 +318,6 @@ __device__ __forceinline__ float load1(const void* buf, const uint32_t* pen, boo
   return x;
 }
 
-// Noise of global token j under the Philox tree (any CTA can evaluate it).
-__device__ __forceinline__ float tree_noise(const NoiseKey& key, const NoiseRoot& root, int64_t gid_s,
-                                            int mem_s, int64_t j, int64_t V) {
-  int s = 0;
-  while (s + 1 < kNumSlices && slice_start(s + 1, V) <= j) ++s;
-  const int64_t a = slice_start(s, V), L = slice_start(s + 1, V) - a;
-  const int64_t o = j - a, lg = local_group(o);
-  const GroupNoise gm = noise_group(key, root, slice_group_base(s, V) + lg, int(group_size(lg, L)), gid_s, mem_s);
-  return noise_token(key, gm, j, member_index(o));
-}
 
 // Bitonic sort (descending) of n = power of two 64-bit keys in shared memory.
 template <int NT>
@@ -340,7 +359,7 @@ __device__ __noinline__ void cluster_exact(const FusedParams& P, int64_t row, cg
   long long* pub = reinterpret_cast<long long*>(scratch + 384);        // published scalars [8]
   const int q = int(cluster.block_rank());
   const unsigned long long Sfix = __double2ull_rn(rs.S * kSumScale);
-  auto fixe = [&](float x) { return (unsigned long long)__double2ull_rn(double(unnorm(x, c1, nM)) * kSumScale); };
+  auto fixe = [&](float x) { return (unsigned long long)__double2ull_rn(double(unnorm_ftz(x, c1, nM)) * kSumScale); };
 
   uint32_t prefix = 0, msk = 0;
   long long cbase = 0;
@@ -509,7 +528,7 @@ __device__ __noinline__ void cluster_exact(const FusedParams& P, int64_t row, cg
     const int64_t j = cta_start + off;
     const bool in = !have || kq > vkey || (kq == vkey && j <= id_c);
     if (in && x > -INFINITY) {
-      const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
+      const float pv = __fdiv_rn(unnorm_ftz(x, c1, nM), Sf);
       const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + j) : tree_noise(key, rt, gs, mem_s, j, V);
       const float rv = __fdiv_rn(pv, E);
       if (rbetter(rv, int(j), br, bid)) { br = rv; bid = int(j); }
@@ -573,7 +592,7 @@ __device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg
   const int i0 = threadIdx.x * per;
   double local = 0.0;
   for (int i = i0; i < i0 + per && i < n; ++i)
-    local += double(__fdiv_rn(unnorm(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
+    local += double(__fdiv_rn(unnorm_ftz(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
   double incl = local;
   for (int o = 1; o < 32; o <<= 1) {
     const double v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -589,7 +608,7 @@ __device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg
     const bool ok = (!rs.p_on || run <= double(rs.tp)) && (!rs.k_on || i < rs.k);
     if (!ok) break;
     ++kept;
-    run += double(__fdiv_rn(unnorm(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
+    run += double(__fdiv_rn(unnorm_ftz(key_to_float(uint32_t(keys[i] >> 32)), c1, nM), Sf));
   }
   const bool complete = kept == max(0, min(per, n - i0));
   const unsigned bal = __ballot_sync(0xffffffffu, !complete);
@@ -617,7 +636,7 @@ __device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg
   for (int i = threadIdx.x; i < nK; i += NT) {
     const float x = key_to_float(uint32_t(keys[i] >> 32));
     const int id = int(0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFu));
-    const float pv = __fdiv_rn(unnorm(x, c1, nM), Sf);
+    const float pv = __fdiv_rn(unnorm_ftz(x, c1, nM), Sf);
     const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + id) : tree_noise(key, rt, gs, mem_s, id, V);
     const float r = __fdiv_rn(pv, E);
     if (rbetter(r, id, br, bid)) { br = r; bid = id; }
@@ -643,7 +662,7 @@ __device__ __noinline__ void gather_finish(const FusedParams& P, int64_t row, cg
 
 // ---------------------------------------------------------------- the kernel
 template <typename T, int CL>
-__global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(FusedParams P) {
+__global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(FusedParams P) {
   constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW, U = Cfg<CL>::U;
   using SM = Smem<T, CL>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -656,6 +675,8 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
   Cand* wl_all = reinterpret_cast<Cand*>(smem + SM::wl_off(P.cap));
   RowState& rs = *reinterpret_cast<RowState*>(smem + SM::rs_off(P.cap));
   Misc& ms = *reinterpret_cast<Misc*>(smem + SM::misc_off(P.cap));
+  GNoise* gnz = reinterpret_cast<GNoise*>(smem + SM::gnz_off(P.cap));
+  Rec1* inbox = reinterpret_cast<Rec1*>(smem + SM::inbox_off(P.cap));   // [2][CL]
 
   cg::cluster_group cluster = cg::this_cluster();
   const int q = int(cluster.block_rank());
@@ -716,6 +737,23 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
         }
       }
     }
+    // the Philox key and the noise root (one lane of the last warp)
+    NoiseKey nkey{0, 0, 0, 0, 0};
+    if (need_race && !parity) {
+      const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
+      nkey = make_noise_key(a.seed, step, a.row_offset + row);
+      if (threadIdx.x == NT - 1) {
+        const NoiseRoot rt = noise_root(nkey, V);
+        int g = 0;
+#pragma unroll
+        for (int st = 8; st >= 1; st >>= 1)
+          if (g + st < kNumSlices && ms.tstart[g + st] <= rt.s) g += st;
+        const int64_t o = rt.s - ms.tstart[g];
+        ms.e_root = rt.e_root;
+        ms.s_gid = ms.tgbase[g] + local_group(o);
+        ms.s_mem = member_index(o);
+      }
+    }
     {
       const T* src = reinterpret_cast<const T*>(src_row) + geo.cta_start;
       T* dst = static_cast<T*>(data);
@@ -735,34 +773,46 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
         }
       }
     }
+    // exact noise of this lane's groups: independent of the logits, so it
+    // overlaps the bulk copy
+    if (need_race && !parity) {
+      const NoiseRoot rt{ms.e_root, 0};
+      const int64_t gid_s0 = ms.s_gid;
+      const int mem_s0 = ms.s_mem;
+#pragma unroll
+      for (int k = 0; k < kMaxItems; ++k) {
+        const int item = warp + k * NW;
+        if (item < geo.nitems) {
+          int u, p;
+          item_of(geo, item, u, p);
+          const Unit un = unit_of(geo, u);
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * p + tt;
+            const int lg = t * 32 + lane;
+            const int n = t < un.ntiles ? group_size(lg, un.L) : 0;
+            if (n > 0) {
+              const GroupNoise gn = noise_group(nkey, rt, un.gbase + lg, n, gid_s0, mem_s0);
+              gnz[threadIdx.x * kSlots + 2 * k + tt] = GNoise{gn.e_min, gn.e2, gn.arg | ((gn.arg2 & 0xFF) << 8)};
+            }
+          }
+        }
+      }
+    }
     if (bulk) {
       if (!mbar_wait(&ms.mbar, phase, kWaitLimit)) ms.err = 1;
       phase ^= 1u;
     }
     __syncthreads();
 
-    // the noise root (one lane of the last warp, overlapping pass 1)
-    if (threadIdx.x == NT - 1 && need_race && !parity) {
-      const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
-      const NoiseKey nk = make_noise_key(a.seed, step, a.row_offset + row);
-      const NoiseRoot rt = noise_root(nk, V);
-      int g = 0;
-#pragma unroll
-      for (int st = 8; st >= 1; st >>= 1)
-        if (g + st < kNumSlices && ms.tstart[g + st] <= rt.s) g += st;
-      const int64_t o = rt.s - ms.tstart[g];
-      ms.e_root = rt.e_root;
-      ms.s_gid = ms.tgbase[g] + local_group(o);
-      ms.s_mem = member_index(o);
-    }
     // ------------------------------------------------------------ pass 1: group max and group-relative sums
-    float gmax[kSlots], fsum[kSlots], gE[kSlots];
+    float gmax[kSlots], fsum[kSlots];
     bool lnan = false;
 #pragma unroll
     for (int k = 0; k < kMaxItems; ++k) {
       const int item = warp + k * NW;
 #pragma unroll
-      for (int tt = 0; tt < 2; ++tt) { gmax[2 * k + tt] = -INFINITY; fsum[2 * k + tt] = 0.f; gE[2 * k + tt] = INFINITY; }
+      for (int tt = 0; tt < 2; ++tt) { gmax[2 * k + tt] = -INFINITY; fsum[2 * k + tt] = 0.f; }
       if (item < geo.nitems) {
         int u, p;
         item_of(geo, item, u, p);
@@ -805,10 +855,11 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
               }
             }
             gmax[2 * k + tt] = m;
-            gE[2 * k + tt] = em;
+            if (parity && need_race) gnz[threadIdx.x * kSlots + 2 * k + tt].e_min = em;
             if (!greedy && m > -INFINITY && m < INFINITY) {
               const float c0g = max_coef(m, c1);
-              float fs = 0.f;
+              // one partial sum per 8-element block (four independent chains)
+              float fb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
               for (int b = 0; b < 4; ++b) {
                 const int local = t * kTile + b * 256 + lane * 8;
@@ -819,10 +870,10 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
                   Load8<T>::run(data, off, nv, x);
                   if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
 #pragma unroll
-                  for (int i = 0; i < 8; ++i) fs = __fadd_rn(fs, unnorm(x[i], c1, c0g));
+                  for (int i = 0; i < 8; ++i) fb[b] = __fadd_rn(fb[b], unnorm_ftz(x[i], c1, c0g));
                 }
               }
-              fsum[2 * k + tt] = fs;
+              fsum[2 * k + tt] = __fadd_rn(__fadd_rn(fb[0], fb[1]), __fadd_rn(fb[2], fb[3]));
             }
           }
         }
@@ -838,6 +889,17 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
                      ms.umaxkey[1] ? key_to_float(ms.umaxkey[1]) : -INFINITY};
     const float cmax = fmaxf(umax[0], umax[1]);
     const float c0 = max_coef(cmax, c1);
+    {
+      // this CTA's softmax sum in its own scale: sum_G fsum(G) 2^(c0 - c0_G)
+      double sp = 0.0;
+      if (!greedy && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY) {
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s)
+          if (fsum[s] > 0.f) sp += double(__fmul_rn(fsum[s], qe_ex2_ftz(__fsub_rn(c0, max_coef(gmax[s], c1)))));
+      }
+      for (int o = 16; o; o >>= 1) sp += __shfl_xor_sync(0xffffffffu, sp, o);
+      if (lane == 0) ms.wS[warp] = sp;
+    }
     const bool race_ok = need_race && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY;
 
     // greedy: first id holding the CTA max (NaN first if any).  Needed for
@@ -927,19 +989,10 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
     const int Rloc = filtered ? 2 : 1;   // tokens a CTA publishes
     const int Rr = filtered ? 3 : 1;     // per-warp list length (one more for the ceiling)
     float bnd[kSlots];
-    float gn_min[kSlots], gn_e2[kSlots];   // exact group noise of the lane's groups
-    int gn_arg[kSlots];                    // argmin | second member << 8
     unsigned done_mask = 0;
 #pragma unroll
-    for (int s = 0; s < kSlots; ++s) { bnd[s] = -1.f; gn_min[s] = 1.f; gn_e2[s] = 1.f; gn_arg[s] = 0; }
-    float e_root = 0.f;
-    int64_t gid_s = -1;
-    int mem_s = 0;
-    NoiseKey nkey{0, 0, 0, 0, 0};
+    for (int s = 0; s < kSlots; ++s) bnd[s] = -1.f;
     if (race_ok) {
-      const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
-      nkey = make_noise_key(a.seed, step, a.row_offset + row);
-      if (!parity) { e_root = ms.e_root; gid_s = ms.s_gid; mem_s = ms.s_mem; }
 #pragma unroll
       for (int k = 0; k < kMaxItems; ++k) {
         const int item = warp + k * NW;
@@ -954,17 +1007,14 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
             const int lg = t * 32 + lane;
             const int n = t < un.ntiles ? group_size(lg, un.L) : 0;
             if (n > 0 && gmax[s] > -INFINITY) {
-              const float emax = unnorm(gmax[s], c1, c0);
+              const float emax = unnorm_ftz(gmax[s], c1, c0);
+              const GNoise g = gnz[threadIdx.x * kSlots + s];
               if (parity) {
-                bnd[s] = __fdividef(emax, gE[s]);
+                bnd[s] = __fdividef(emax, g.e_min);
               } else {
-                const GroupNoise gn = noise_group(nkey, NoiseRoot{e_root, 0}, un.gbase + lg, n, gid_s, mem_s);
-                gn_min[s] = gn.e_min;
-                gn_e2[s] = gn.e2;
-                gn_arg[s] = gn.arg | ((gn.arg2 & 0xFF) << 8);
-                const float xa = load1<T>(data, pen, use_pen, rpv, un.uoff + int(member_offset(lg, gn.arg)));
-                float b = __fdividef(unnorm(xa, c1, c0), gn.e_min);
-                if (n >= 2) b = fmaxf(b, __fdividef(emax, gn.e2));
+                const float xa = load1<T>(data, pen, use_pen, rpv, un.uoff + int(member_offset(lg, g.args & 0xFF)));
+                float b = __fdividef(unnorm_ftz(xa, c1, c0), g.e_min);
+                if (n >= 2) b = fmaxf(b, __fdividef(emax, g.e2));
                 bnd[s] = b;
               }
             }
@@ -984,19 +1034,19 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
       const int lg = t * 32 + ol;
       const int local = int(member_offset(lg, lane));
       // the owner lane's exact group noise
+      const GNoise g = gnz[(warp * 32 + ol) * kSlots + s];
       GroupNoise gn;
-      gn.e_min = __shfl_sync(0xffffffffu, s ? gn_min[1] : gn_min[0], ol);
-      gn.e2 = __shfl_sync(0xffffffffu, s ? gn_e2[1] : gn_e2[0], ol);
-      const int ga = __shfl_sync(0xffffffffu, s ? gn_arg[1] : gn_arg[0], ol);
-      gn.arg = ga & 0xFF;
-      gn.arg2 = ((ga >> 8) & 0xFF) == 0xFF ? -1 : ((ga >> 8) & 0xFF);
+      gn.e_min = g.e_min;
+      gn.e2 = g.e2;
+      gn.arg = g.args & 0xFF;
+      gn.arg2 = ((g.args >> 8) & 0xFF) == 0xFF ? -1 : ((g.args >> 8) & 0xFF);
       float r = -INFINITY, x = 0.f, E = 1.f;
       int id = 0x7FFFFFFF;
       if (local < un.L) {
         x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
         id = int(geo.cta_start + un.uoff + local);
         E = parity ? __ldg(a.noise + row * a.noise_ld + id) : noise_token(nkey, gn, id, lane);
-        r = __fdiv_rn(unnorm(x, c1, c0), E);
+        r = __fdiv_rn(unnorm_ftz(x, c1, c0), E);
         if (r != r) r = -INFINITY;
       }
       warp_merge(wl, Rr, r, x, E, id);
@@ -1043,22 +1093,11 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
       for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
       if (lane == 0) ms.wceil[warp] = cm;
     }
-    {
-      // this CTA's softmax sum in its own scale: sum_G fsum(G) 2^(c0 - c0_G)
-      double sp = 0.0;
-      if (!greedy && !cnan && cmax > -INFINITY && fabsf(c0) < INFINITY) {
-#pragma unroll
-        for (int s = 0; s < kSlots; ++s)
-          if (fsum[s] > 0.f) sp += double(__fmul_rn(fsum[s], qe_ex2(__fsub_rn(c0, max_coef(gmax[s], c1)))));
-      }
-      for (int o = 16; o; o >>= 1) sp += __shfl_xor_sync(0xffffffffu, sp, o);
-      if (lane == 0) ms.wS[warp] = sp;
-    }
     __syncthreads();
 
     // ------------------------------------------------------------ exchange 1: maxima, greedy, sum, race candidates
     {
-      Share& my = share[ex & 1];
+      Rec1& my = inbox[(ex & 1) * CL + q];
       if (warp == 0) {
         // the CTA's best Rloc tokens and the ceiling over everything else
         constexpr int PER = (NW * 3 + 31) / 32;
@@ -1079,15 +1118,9 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
           Cand cb = c[0];
 #pragma unroll
           for (int i = 1; i < PER; ++i) if (i == bi) cb = c[i];
-          float br = cb.r; int bid = cb.id; int bl = lane;
-          for (int o = 16; o; o >>= 1) {
-            const float orr = __shfl_xor_sync(0xffffffffu, br, o);
-            const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            if (rbetter(orr, oid, br, bid)) { br = orr; bid = oid; bl = ol; }
-          }
-          if (!(br > -INFINITY)) break;
-          if (round == Rloc) { third = br; break; }
+          const int bl = warp_best_lane(cb.r, cb.id);
+          if (bl < 0) break;
+          if (round == Rloc) { third = __shfl_sync(0xffffffffu, cb.r, bl); break; }
           if (lane == bl) {
             my.cand[n] = cb;
 #pragma unroll
@@ -1112,6 +1145,15 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
           my.gval = cnan ? NAN : cmax;
           my.lkey = topk_lkey;
         }
+        __syncwarp();
+        // push the record into every peer's inbox (DSMEM stores; the cluster
+        // barrier below orders them before the peers' reads)
+        if (lane < CL && lane != q) {
+          const uint4* src = reinterpret_cast<const uint4*>(&my);
+          uint4* dst = reinterpret_cast<uint4*>(cluster.map_shared_rank(&my, lane));
+#pragma unroll
+          for (int i = 0; i < int(sizeof(Rec1) / 16); ++i) dst[i] = src[i];
+        }
       }
       cluster.sync();
       if (warp == 0) {
@@ -1123,7 +1165,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
         Cand pc[2];
         pc[0] = pc[1] = Cand{-INFINITY, 0.f, 1.f, 0x7FFFFFFF};
         if (lane < CL) {
-          const Share* sp = cluster.map_shared_rank(&share[ex & 1], lane);
+          const Rec1* sp = &inbox[(ex & 1) * CL + lane];
           for (int u = 0; u < U; ++u) pm = fmaxf(pm, sp->umax[u]);
           pc0 = sp->c0; pn = sp->nan; gi = sp->gidx; gv = sp->gval; lk = sp->lkey; pnc = sp->ncand;
           pS = sp->S; pceil = sp->ceil;
@@ -1131,8 +1173,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
           if (pnc > 1) pc[1] = sp->cand[1];
         }
         const bool anynan = __any_sync(0xffffffffu, pn != 0);
-        float xM = pm;
-        for (int o = 16; o; o >>= 1) xM = fmaxf(xM, __shfl_xor_sync(0xffffffffu, xM, o));
+        const float xM = key_to_float(__reduce_max_sync(0xffffffffu, ordered_key(pm)));
         for (int o = 16; o; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
           const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
@@ -1141,35 +1182,27 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
         lk = __reduce_max_sync(0xffffffffu, lk);
         const float nM = max_coef(xM, c1);
         // row scale: a CTA's ratios and sum times 2^(nM - c0_cta)
-        const double sc = (lane < CL && pnc >= 0 && fabsf(pc0) < INFINITY) ? exp2(double(nM) - double(pc0)) : 0.0;
+        const double sc = (lane < CL && fabsf(pc0) < INFINITY) ? double(qe_ex2_ftz(__fsub_rn(nM, pc0))) : 0.0;
         double Sv = lane < CL ? pS * sc : 0.0;
         for (int o = 16; o; o >>= 1) Sv += __shfl_xor_sync(0xffffffffu, Sv, o);
-        double phi = double(pceil) * sc;
-        for (int o = 16; o; o >>= 1) phi = fmax(phi, __shfl_xor_sync(0xffffffffu, phi, o));
-        double pr[2];
+        const float scf = float(sc);
+        // ceilings are >= 0: their bit patterns order like the values
+        const float phif = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lane < CL ? pceil * scf : 0.f)));
 #pragma unroll
-        for (int i = 0; i < 2; ++i) pr[i] = pc[i].r > -INFINITY ? double(pc[i].r) * sc : -1.0;
+        for (int i = 0; i < 2; ++i) pc[i].r = pc[i].r > -INFINITY ? pc[i].r * scf : -INFINITY;
         int n = 0, ncomplete = 0;
         for (int round = 0; round < kMaxR; ++round) {
-          const int bi = (pr[1] > pr[0] || (pr[1] == pr[0] && pc[1].id < pc[0].id)) ? 1 : 0;
-          double bv = bi ? pr[1] : pr[0];
-          int bid = bi ? pc[1].id : pc[0].id;
-          int bl = lane;
-          for (int o = 16; o; o >>= 1) {
-            const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-            const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            if (ov > bv || (ov == bv && (oid < bid || (oid == bid && ol < bl)))) { bv = ov; bid = oid; bl = ol; }
-          }
-          if (!(bv >= 0.0) || bid == 0x7FFFFFFF) break;
+          const int bi = rbetter(pc[1].r, pc[1].id, pc[0].r, pc[0].id) ? 1 : 0;
+          const Cand cb = bi ? pc[1] : pc[0];
+          const int bl = warp_best_lane(cb.r, cb.id);
+          if (bl < 0) break;
+          const float br = __shfl_sync(0xffffffffu, cb.r, bl);
           if (lane == bl) {
-            Cand cb = bi ? pc[1] : pc[0];
-            cb.r = float(bv);
             rs.cand[n] = cb;
-            if (bi) { pr[1] = -1.0; pc[1].id = 0x7FFFFFFF; } else { pr[0] = -1.0; pc[0].id = 0x7FFFFFFF; }
+            if (bi) pc[1].r = -INFINITY; else pc[0].r = -INFINITY;
           }
           ++n;
-          if (bv > phi) ncomplete = n;   // no unpublished token can beat it
+          if (br > phif) ncomplete = n;   // no unpublished token can beat it
         }
         __syncwarp();
         if (lane == 0) {
@@ -1271,7 +1304,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
                 for (int i = 0; i < 8; ++i) {
                   if (x[i] > thmin) {
                     // a token is ahead of candidate c iff (x, -id) > (x_c, -id_c)
-                    const float e = unnorm(x[i], c1, nM);
+                    const float e = unnorm_ftz(x[i], c1, nM);
 #pragma unroll
                     for (int c = 0; c < kMaxR; ++c) {
                       if (c < R && (x[i] > cv[c] || (x[i] == cv[c] && id0 + i < cidv[c]))) { Fl[c] += e; Cl[c] += 1; }
@@ -1326,32 +1359,26 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 3 : 2) fused_kernel(Fu
         int ngat = 0, ovf = 0;
         for (int r = 0; r < CL; ++r) { ngat += peers[r].ngather; ovf |= peers[r].overflow; }
         if (do_test) {
-          double F[kMaxR];
-          long long C[kMaxR];
-          for (int c = 0; c < kMaxR; ++c) { F[c] = 0.0; C[c] = 0; }
-          for (int r = 0; r < CL; ++r)
-            for (int c = 0; c < R; ++c) { F[c] += peers[r].F[c]; C[c] += peers[r].cnt[c]; }
-          // exact ratios; the first candidate in race order inside the kept set wins
-          float rM[kMaxR];
-          int order[kMaxR];
-          for (int c = 0; c < R; ++c) {
-            rM[c] = __fdiv_rn(__fdiv_rn(unnorm(rs.cand[cb + c].x, c1, nM), rs.Sf), rs.cand[cb + c].E);
-            order[c] = c;
-          }
-          for (int i = 1; i < R; ++i) {
-            const int v = order[i];
-            int j = i;
-            while (j > 0 && rbetter(rM[v], rs.cand[cb + v].id, rM[order[j - 1]], rs.cand[cb + order[j - 1]].id)) {
-              order[j] = order[j - 1]; --j;
-            }
-            order[j] = v;
-          }
+          // exact ratios; the first candidate in race order inside the kept
+          // set wins (selection over a bit mask: no local arrays)
+          unsigned left = (1u << R) - 1u;
           int win = -1;
           float Lx = rs.L;
-          for (int i = 0; i < R; ++i) {
-            const int c = order[i];
-            const bool okp = !p_on || F[c] <= double(tp) * rs.S;
-            const bool okk = !k_on || C[c] < kk;
+          while (left) {
+            int c = -1;
+            float rc = 0.f;
+            for (int i = 0; i < R; ++i) {
+              if (!((left >> i) & 1u)) continue;
+              const Cand& ci = rs.cand[cb + i];
+              const float ri = __fdiv_rn(__fdiv_rn(unnorm_ftz(ci.x, c1, nM), rs.Sf), ci.E);
+              if (c < 0 || rbetter(ri, ci.id, rc, rs.cand[cb + c].id)) { c = i; rc = ri; }
+            }
+            left &= ~(1u << c);
+            double Fc = 0.0;
+            long long Cc = 0;
+            for (int r = 0; r < CL; ++r) { Fc += peers[r].F[c]; Cc += peers[r].cnt[c]; }
+            const bool okp = !p_on || Fc <= double(tp) * rs.S;
+            const bool okk = !k_on || Cc < kk;
             if (okp && okk) { win = c; break; }
             Lx = fmaxf(Lx, rs.cand[cb + c].x);
           }
@@ -1464,7 +1491,7 @@ int fused_capacity(int64_t V, int cluster) {
     const int64_t n = slice_start(q * U + U, V) - slice_start(q * U, V);
     if (n > mx) mx = n;
   }
-  int64_t cap = ((mx + 1023) / 1024) * 1024 + 1024;
+  int64_t cap = ((mx + 1023) / 1024) * 1024;
   if (cap < 8192) cap = 8192;  // room for CTA 0 to sort >= 1024 gathered keys
   const int NW = cluster == 8 ? 16 : 8;
   // every warp owns at most kMaxItems tile pairs
