@@ -5,15 +5,19 @@ B=256, V=248,320 (config 3: bf16 Zipf logits, top_p=0.95, T=1.0, Philox
 noise), and the fraction of the HBM roofline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 3] [--mode philox|noise]
+                    [--config 3] [--mode philox|noise] [--vocab-sharded]
 
 A step is one sampler call over one batch of B rows resident in HBM.  L2 is
 not allowed to serve the logits: the timed loop rotates over enough distinct
 logits buffers to exceed twice the L2 size.  Multi-GPU (torchrun, NCCL):
 rows are sharded with no data-path collective (weak scaling: every rank
 samples its own B rows, keyed on its global row offset); time is the max
-over ranks.  ``--impl reference`` times the reference algorithm's CPU
-restatement (oracle/) on the host cores, rank 0 only.
+over ranks.  ``--vocab-sharded`` (config 5 by default) instead splits the
+vocabulary over the ranks (tensor-parallel lm_head): every rank holds
+``[B, V/N]`` of the same rows and the shards are merged by NCCL all-gathers
+of per-slice records (strong scaling).  ``--impl reference`` times the
+reference algorithm's CPU restatement (oracle/) on the host cores, rank 0
+only.
 """
 from __future__ import annotations
 
@@ -130,6 +134,101 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_vocab_sharded(args, rank: int, world: int, local: int):
+    """Config 5: every rank samples the same B rows from its vocab shard."""
+    import torch
+    import torch.distributed as dist
+    from qedge_b200 import workloads as W
+    from qedge_b200.sharded import ShardedSampler, shard_bounds
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    w = W.CONFIGS[args.config]()
+    B, V = w.B, w.V
+    v0, v1 = shard_bounds(V, world, rank)
+    esize = 4 if w.dtype == "f32" else 2
+    shard_bytes = B * (v1 - v0) * esize
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / shard_bytes)) + 1)
+    full = W.to_device(w, dev)
+    bufs = [full[:, v0:v1].roll(shifts=i * 997, dims=1).contiguous() for i in range(nbuf)]
+    del full
+    temps = torch.from_numpy(w.temperatures).to(dev)
+    tps = torch.from_numpy(w.top_ps).to(dev)
+    tks = torch.from_numpy(w.top_ks.astype(np.int32)).to(dev)
+    if world > 1:
+        sampler = ShardedSampler(1234, nshards=world, shard=rank)
+    else:
+        sampler = ShardedSampler(1234, nshards=1, shard=0, allgather=lambda t: t)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, buf=None):
+        return sampler(bufs[i % nbuf] if buf is None else buf, V, temps, tps, use_top_p=w.use_top_p,
+                       top_ks=tks, step=i)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    with clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    total_ms = ev0.elapsed_time(ev1)
+    host = torch.empty_like(bufs[0], device="cpu").pin_memory()
+    host.copy_(bufs[0])
+    out_host = torch.empty(B, dtype=torch.int64).pin_memory()
+    dbuf = torch.empty_like(bufs[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(max(args.e2e_steps, 1)):
+        dbuf.copy_(host, non_blocking=True)
+        out_host.copy_(step(10_000 + i, dbuf), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / max(args.e2e_steps, 1)
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0].item()), float(t[1].item())
+    ms = total_ms / args.steps
+    hbm, peak_kind = peaks()
+    alg = shard_bytes + 8 * B
+    achieved = alg / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": f"sampled rows/sec, config {args.config} vocab-sharded over {world} GPU(s)",
+            "value": B / (ms * 1e-3), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": w.dtype + " in, f32 math", "data": "synthetic",
+            "config": {"workload": w.name, "B": B, "V": V, "noise": "philox",
+                       "parallelism": f"vocab x{world} (NCCL all-gather of slice records)",
+                       "l2": f"rotating {nbuf} shard buffers per rank"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
+                         "alg_bytes_per_launch": alg, "note": "per rank, whole step incl. collectives"},
+            "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": shard_bytes,
+                    "d2h_bytes_per_step": 8 * B},
+            "gpu_launches": args.steps * 4,
+            "fallback_rows": sampler.fallback_rows,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -140,7 +239,10 @@ def main():
     ap.add_argument("--mode", default="philox", choices=["philox", "noise"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--vocab-sharded", action="store_true")
     args = ap.parse_args()
+    if args.vocab_sharded and "--config" not in sys.argv:
+        args.config = 5
     args.warmup = max(args.warmup, 3)
 
     rank = int(os.environ.get("RANK", "0"))
@@ -148,6 +250,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.vocab_sharded:
+        return run_vocab_sharded(args, rank, world, local)
 
     import torch
     import torch.distributed as dist

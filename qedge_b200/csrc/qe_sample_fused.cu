@@ -684,7 +684,11 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   Cand* wl = wl_all + warp * kMaxR;
   const int64_t V = a.vocab;
-  const Geo geo = make_geo<U>(q, V);
+  // the CTA's slice geometry lives in shared memory (read where needed)
+  __shared__ Geo geo_s;
+  if (threadIdx.x == 0) geo_s = make_geo<U>(q, V);
+  __syncthreads();
+  const Geo& geo = geo_s;
   const int n_cta = int(geo.cta_end - geo.cta_start);
   int ex = 0;
 
