@@ -192,7 +192,9 @@ __device__ __forceinline__ GroupNoise group_noise_from(const NoiseRoot& root, U4
     g.e_min = root.e_root;
     g.arg = mem_s;
   } else {
-    g.e_min = __fadd_rn(root.e_root, __fdiv_rn(neglog(uniform_open(w.x)), float(n)));
+    // n = 32 (every full group): the division is an exact scaling by 2^-5
+    const float l = neglog(uniform_open(w.x));
+    g.e_min = __fadd_rn(root.e_root, n == 32 ? __fmul_rn(l, 0.03125f) : __fdiv_rn(l, float(n)));
     g.arg = int(select_index32(w.y, uint32_t(n)));
   }
   if (n >= 2) {
