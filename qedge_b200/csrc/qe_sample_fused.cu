@@ -45,6 +45,7 @@ constexpr int kSlots = 2 * kMaxItems;  // groups per lane
 static_assert(kSlots == 2, "slot selects below assume one tile pair per warp");
 constexpr int kGatherCap = 768;   // gathered keys per CTA
 constexpr int kSmallK = 64;       // top-k rows up to this k take the gather path
+constexpr int kSparseGroups = 12; // candidate tests: tiles with at most this many active groups go group by group
 constexpr uint32_t kWaitLimit = 1u << 20;   // polls (each suspends up to 1 us)
 
 enum RowType : int { kDone = 0, kRaceTest = 1, kGather = 2, kSlow = 3 };
@@ -126,6 +127,7 @@ struct Misc {
   long long s_gid;
   unsigned int wtop[16 * 8];
   float theta;           // running race threshold of the CTA (positive floats as ints)
+  float wbound[16];      // each warp's largest group bound
   float wceil[16];
   float wb[16];
   int wbslot[16];
@@ -1061,6 +1063,35 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
       // warps' own Rloc-th bests, which never exceeds the CTA's).
       volatile float* th_cta = &ms.theta;
       volatile float* wbest = ms.wb;
+      // Seeds: only the Rloc warps holding the CTA's largest bounds expand
+      // before a threshold exists (the others would expand blindly).
+      {
+        float mb = fmaxf(bnd[0], bnd[1]);
+        mb = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(mb, 0.f))));
+        if (lane == 0) ms.wbound[warp] = mb;
+        __syncthreads();
+        float b1 = 0.f, b2 = 0.f;
+        for (int w = 0; w < NW; ++w) {
+          const float v = ms.wbound[w];
+          if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+        }
+        const float cut = Rloc == 1 ? b1 : b2;
+        if (mb > 0.f && mb >= cut) {
+          int bs = bnd[1] > bnd[0] ? 1 : 0;
+          const float bb = bs ? bnd[1] : bnd[0];
+          int code = bb == mb ? lane * 8 + bs : 0x7FFFFFFF;
+          code = int(__reduce_min_sync(0xffffffffu, uint32_t(code)));
+          if (code != 0x7FFFFFFF) {
+            if (lane == (code >> 3)) done_mask |= 1u << (code & 7);
+            eval_group(code & 7, code >> 3);
+            __syncwarp();
+            const float mine = wl[Rloc - 1].r;
+            if (lane == 0 && mine > 0.f) atomicMax(reinterpret_cast<int*>(&ms.theta), __float_as_int(mine));
+            if (lane == 0) wbest[warp] = wl[0].r;
+          }
+        }
+        __syncthreads();
+      }
       for (;;) {
         float theta = fmaxf(*th_cta, wl[Rloc - 1].r);
         if (Rloc == 2) {
@@ -1293,7 +1324,27 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
           const float gm = tt ? gmax[1] : gmax[0];
           const bool q_test = do_test && t < un.ntiles && gm > thmin;
           const bool q_gath = do_gather && t < un.ntiles && gm >= Lg;
-          if (__any_sync(0xffffffffu, q_test || q_gath)) {
+          const uint32_t tmask = __ballot_sync(0xffffffffu, q_test);
+          if (do_test && __popc(tmask) <= kSparseGroups) {
+            // few active groups: the warp walks them one at a time, lane m
+            // on member m (each group costs one pass instead of a tile's four)
+            uint32_t mleft = tmask;
+            while (mleft) {
+              const int ol = __ffs(mleft) - 1;
+              mleft &= mleft - 1;
+              const int local = int(member_offset(t * 32 + ol, lane));
+              if (local < un.L) {
+                const float x = load1<T>(data, pen, use_pen, rpv, un.uoff + local);
+                if (x > thmin) {
+                  const int id = int(geo.cta_start) + un.uoff + local;
+                  const float e = unnorm_ftz(x, c1, nM);
+#pragma unroll
+                  for (int c = 0; c < kMaxR; ++c)
+                    if (c < R && (x > cv[c] || (x == cv[c] && id < cidv[c]))) { Fl[c] += e; Cl[c] += 1; }
+                }
+              }
+            }
+          } else if (__any_sync(0xffffffffu, q_test || q_gath)) {
 #pragma unroll 1
             for (int b = 0; b < 4; ++b) {
               const int local = t * kTile + b * 256 + lane * 8;
