@@ -26,7 +26,8 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 // Bounded wait on an mbarrier phase.  Returns false if the phase did not
 // complete within `limit` polls (the caller records an error; it never hangs).
 // Each poll may suspend the thread for up to kTryWaitHintNs (it resumes as
-// soon as the phase completes), so the bound is limit * kTryWaitHintNs.
+// soon as the phase completes) and sleeps 128 ns after a miss, so the bound
+// is about limit * (kTryWaitHintNs + 128 ns).
 constexpr uint32_t kTryWaitHintNs = 1000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
   uint32_t done = 0;
@@ -37,6 +38,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
         : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitHintNs)
         : "memory");
     if (done) return true;
+    __nanosleep(128);   // fewer polls while the copy is in flight
   }
   return false;
 }

@@ -824,9 +824,39 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
         item_of(geo, item, u, p);
         const Unit un = unit_of(geo, u);
 #pragma unroll
+        // common case: both tiles complete, no penalty, Philox noise -- every
+        // block holds 8 valid elements and needs no per-element checks
+        const bool lean = !use_pen && !(parity && need_race) && (2 * p + 2) * kTile <= un.L;
+        if (lean) {
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * p + tt;
+            float m = -INFINITY;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const float mb = Max8<T>::run(data, un.uoff + t * kTile + b * 256 + lane * 8, 8);
+              lnan |= (mb != mb);
+              m = fmaxf(m, mb);
+            }
+            gmax[2 * k + tt] = m;
+            if (!greedy && m > -INFINITY && m < INFINITY) {
+              const float c0g = max_coef(m, c1);
+              float fb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                float x[8];
+                Load8<T>::run(data, un.uoff + t * kTile + b * 256 + lane * 8, 8, x);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) fb[b] = __fadd_rn(fb[b], unnorm_ftz(x[i], c1, c0g));
+              }
+              fsum[2 * k + tt] = __fadd_rn(__fadd_rn(fb[0], fb[1]), __fadd_rn(fb[2], fb[3]));
+            }
+          }
+        }
+#pragma unroll
         for (int tt = 0; tt < 2; ++tt) {
           const int t = 2 * p + tt;
-          if (t < un.ntiles) {
+          if (!lean && t < un.ntiles) {
             float m = -INFINITY, em = INFINITY;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
