@@ -184,33 +184,26 @@ __device__ __forceinline__ void list_insert(Cand* l, int n, const Cand& c) {
 // (ordered ratio, inverted id) per shuffle step.
 __device__ __forceinline__ void warp_merge(Cand* wl, int n, float r, float x, float E, int id) {
   const int lane = threadIdx.x & 31;
-  float m = r;
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  const float floor_r = wl[n - 1].r;
-  if (!(m >= floor_r) || !(m > -INFINITY)) return;
-  unsigned long long key = r > -INFINITY
-      ? (uint64_t(ordered_key(r)) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(id)) : 0ull;
+  // ratios are >= 0 or -inf: for r >= 0 the bit pattern orders like the value
+  uint32_t k = r >= 0.f ? __float_as_uint(r) + 1u : 0u;
+  const uint32_t floor_k = wl[n - 1].r >= 0.f ? __float_as_uint(wl[n - 1].r) + 1u : 0u;
   for (int round = 0; round < n; ++round) {
-    unsigned long long best = key;
-    for (int o = 16; o; o >>= 1) {
-      const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
-      best = ok > best ? ok : best;
-    }
-    if (best == 0ull) break;
-    const int bl = __ffs(__ballot_sync(0xffffffffu, key == best)) - 1;
-    const float br = __shfl_sync(0xffffffffu, r, bl);
+    const uint32_t km = __reduce_max_sync(0xffffffffu, k);
+    if (km == 0u || km < floor_k) break;
+    const uint32_t im = __reduce_min_sync(0xffffffffu, k == km ? uint32_t(id) : 0xFFFFFFFFu);
+    const int bl = __ffs(__ballot_sync(0xffffffffu, k == km && uint32_t(id) == im)) - 1;
     const float bx = __shfl_sync(0xffffffffu, x, bl);
     const float bE = __shfl_sync(0xffffffffu, E, bl);
-    const int bid = __shfl_sync(0xffffffffu, id, bl);
     bool stop = false;
     if (lane == 0) {
-      stop = !rbetter(br, bid, wl[n - 1].r, wl[n - 1].id);
-      if (!stop) list_insert(wl, n, Cand{br, bx, bE, bid});
+      const float br = __uint_as_float(km - 1u);
+      stop = !rbetter(br, int(im), wl[n - 1].r, wl[n - 1].id);
+      if (!stop) list_insert(wl, n, Cand{br, bx, bE, int(im)});
     }
     stop = __shfl_sync(0xffffffffu, stop, 0);
     __syncwarp();
     if (stop) break;
-    if (lane == bl) key = 0ull;
+    if (lane == bl) k = 0u;
   }
 }
 
@@ -1126,12 +1119,12 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
         float theta = fmaxf(*th_cta, wl[Rloc - 1].r);
         if (Rloc == 2) {
           // the second largest of the warps' bests also bounds the CTA's 2nd
-          float b1 = 0.f, b2 = 0.f;
-          for (int w = 0; w < NW; ++w) {
-            const float v = wbest[w];
-            if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
-          }
-          theta = fmaxf(theta, b2);
+          // (non-negative floats: bit patterns order like the values)
+          const uint32_t v = lane < NW ? __float_as_uint(fmaxf(wbest[lane], 0.f)) : 0u;
+          const uint32_t v1 = __reduce_max_sync(0xffffffffu, v);
+          const int l1 = __ffs(__ballot_sync(0xffffffffu, v == v1)) - 1;
+          const uint32_t v2 = __reduce_max_sync(0xffffffffu, lane == l1 ? 0u : v);
+          theta = fmaxf(theta, __uint_as_float(v2));
         }
         float bb = -1.f;
         int bs = -1;
