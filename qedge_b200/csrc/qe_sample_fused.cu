@@ -1376,7 +1376,15 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
               float x[8];
               Load8<T>::run(data, off, nv, x);
               if (use_pen) apply_penalty8((pen[off >> 5] >> (off & 31)) & 0xFFu, rpv, x);
-              if (q_test) {
+              if (q_test && R == 1) {
+                // one candidate (round 0): a compare, an exponential, two adds
+                const int id0 = int(geo.cta_start) + off;
+                const float v = cv[0];
+                const int cid = cidv[0];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  if (x[i] > v || (x[i] == v && id0 + i < cid)) { Fl[0] += unnorm_ftz(x[i], c1, nM); Cl[0] += 1; }
+              } else if (q_test) {
                 const int id0 = int(geo.cta_start) + off;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
