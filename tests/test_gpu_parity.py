@@ -164,3 +164,19 @@ def test_fallback_paths_vs_oracle(sampler):
     ids = run(sampler, w, None, seed=9, step=2, out_status=st)
     noise = ON.philox_noise(B, V, 9, 2)
     np.testing.assert_array_equal(ids, oracle_ids(w, noise))
+
+
+def test_vocab_beyond_fused_capacity_uses_multikernel_path(monkeypatch):
+    """V above the fused kernel's shared-memory capacity (262,144) is served
+    by the multi-kernel path under the default dispatch, with the same ids."""
+    from qedge_b200.sampler import QESampler
+    monkeypatch.delenv("QE_SAMPLER_PATH", raising=False)
+    V, B = 300_001, 4
+    g = np.random.Generator(np.random.PCG64(17))
+    x = g.standard_normal((B, V), dtype=np.float32) * np.float32(2.0)
+    w = W.Workload("big_v", W.to_bf16_bits(x), "bf16", np.array([0.0, 0.7, 1.0, 1.2], np.float32),
+                   np.array([0.9, 0.9, 0.5, 1.0], np.float32), np.array([0, 0, 40, 0], np.int32),
+                   np.ones(B, np.float32), None, None, use_top_p=True)
+    noise = ON.philox_noise(B, V, 8, 2)
+    ids = run(QESampler(seed=8), w, None, seed=8, step=2)
+    np.testing.assert_array_equal(ids, oracle_ids(w, noise))
