@@ -4,25 +4,30 @@
 // Replaces BatchSampler.forward (src/compute/sampler.py:25-41) for rows
 // whose CTA share fits in shared memory.  Every row is read from HBM once,
 // by 1-D bulk copies (cp.async.bulk + mbarrier), into the shared memory of
-// the 8 (or 16) CTAs of a cluster; CTA q holds canonical vocab slices
-// [qU, qU+U).  Per row:
+// the 8 CTAs (16 on request) of a cluster; CTA q holds canonical vocab
+// slices [qU, qU+U).  Per row:
 //
-//   pass 1   per 32-id group: max, then the canonical softmax sum relative
-//            to the group max (the only pass with an exponential per token)
+//   noise    while the copy flies, each lane computes the exact minimum and
+//            second-smallest noise of its two 32-id groups (one Philox call
+//            per group)
+//   pass 1   per group: max, then the softmax sum relative to the group max
+//            (the only pass with an exponential per token)
 //   race     lazy exponential race: a group's best ratio is bounded by
-//            max(e)/min(E); only groups whose bound can still win are
-//            expanded, using the minimum-first Philox noise tree
-//   exchange candidates over DSMEM (cluster barrier)
-//   pass 2   sparse: only groups whose max lies above a candidate are read,
-//            giving the exact probability mass and rank ahead of it
-//   exchange decide: the first candidate (in race order) inside the
-//            top-k / top-p set wins
+//            max(e_arg / E_min, e_max / E2); each CTA expands, warp by warp,
+//            only groups whose bound reaches its running threshold and so
+//            finds its exact best tokens and a ceiling over the rest
+//   exchange one cluster barrier: each CTA pushes its record (max, sum,
+//            candidates, ceiling) into every peer's shared memory; greedy and
+//            unfiltered rows are decided here
+//   tests    top-k / top-p rows: the best candidate first (groups below it
+//            skipped), then the other complete candidates; each round ends
+//            in a cluster exchange of the mass and rank ahead of them
 //
 // Rows with a small top-k, and the rare rows whose candidates all fall
-// outside the nucleus, gather every token above a proven lower bound of the
+// outside the kept set, gather every token above a proven lower bound of the
 // kept set and finish exactly in CTA 0 (sort + prefix mass + race).  Rows
-// that defeat that too are finished by CTA 0 alone over DSMEM with the
-// radix-select method of the multi-kernel path.
+// whose gathered set is too large are finished by the whole cluster with a
+// radix selection over the CTAs' own slices.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
