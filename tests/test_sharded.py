@@ -212,3 +212,23 @@ def test_nccl_two_gpus_match_single_gpu():
             p.join(300)
         assert all(p.exitcode == 0 for p in procs)
         assert dict(result) == {0: True, 1: True}
+
+
+@pytest.mark.gpu
+def test_sharded_sampler_finishes_slow_rows_exactly():
+    """``ShardedSampler`` (one shard, identity all-gather) finishes the rows the
+    candidate round could not decide by gathering them and running the
+    single-GPU sampler: every id equals the oracle's."""
+    from qedge_b200.sharded import ShardedSampler
+    w = _mixed(B=64, seed=23)
+    dev = "cuda"
+    s = ShardedSampler(9, nshards=1, shard=0, allgather=lambda t: t)
+    st = torch.zeros(w.B, dtype=torch.int32, device=dev)
+    ids = s(W.to_device(w, dev), w.V, torch.from_numpy(w.temperatures).to(dev),
+            torch.from_numpy(w.top_ps).to(dev), use_top_p=True, top_ks=torch.from_numpy(w.top_ks).to(dev),
+            rep_penalties=torch.from_numpy(w.rep_penalties).to(dev), history=torch.from_numpy(w.history).to(dev),
+            history_lens=torch.from_numpy(w.history_lens).to(dev), step=6, out_status=st)
+    torch.cuda.synchronize()
+    noise = ON.philox_noise(w.B, w.V, 9, 6)
+    np.testing.assert_array_equal(ids.cpu().numpy(), _oracle(w, noise))
+    assert s.fallback_rows > 0
