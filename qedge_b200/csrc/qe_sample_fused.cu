@@ -348,7 +348,8 @@ template <typename T, int CL>
 __device__ __noinline__ void cluster_exact(const FusedParams& P, int64_t row, cg::cluster_group& cluster,
                                            const void* data, const uint32_t* pen, unsigned long long* scratch,
                                            const RowState& rs, bool use_pen, float rpv, int64_t cta_start,
-                                           int n_cta, int* s_int, float* s_flt) {
+                                           int n_cta, int* s_int, float* s_flt, const GNoise* gnz,
+                                           const Geo& geo) {
   constexpr int NT = Cfg<CL>::NT, NW = Cfg<CL>::NW;
   const KernelArgs& a = P.a;
   const int64_t V = a.vocab;
@@ -529,7 +530,25 @@ __device__ __noinline__ void cluster_exact(const FusedParams& P, int64_t row, cg
     const bool in = !have || kq > vkey || (kq == vkey && j <= id_c);
     if (in && x > -INFINITY) {
       const float pv = __fdiv_rn(unnorm_ftz(x, c1, nM), Sf);
-      const float E = a.noise ? __ldg(a.noise + row * a.noise_ld + j) : tree_noise(key, rt, gs, mem_s, j, V);
+      float E;
+      if (a.noise) {
+        E = __ldg(a.noise + row * a.noise_ld + j);
+      } else if (gnz) {
+        // the row's group noise is still in the table: only the token word is new
+        const int u = (Cfg<CL>::U == 2 && off >= geo.uoff[1]) ? 1 : 0;
+        const int o = off - (u ? geo.uoff[1] : geo.uoff[0]);
+        const int t = o >> 10, l = (o >> 3) & 31;
+        const int item = (u ? geo.npairs[0] : 0) + (t >> 1);
+        const GNoise g = gnz[(item * 32 + l) * kSlots + (t & 1)];
+        GroupNoise gn;
+        gn.e_min = g.e_min;
+        gn.e2 = g.e2;
+        gn.arg = g.args & 0xFF;
+        gn.arg2 = ((g.args >> 8) & 0xFF) == 0xFF ? -1 : ((g.args >> 8) & 0xFF);
+        E = noise_token(key, gn, j, member_index(o));
+      } else {
+        E = tree_noise(key, rt, gs, mem_s, j, V);
+      }
       const float rv = __fdiv_rn(pv, E);
       if (rbetter(rv, int(j), br, bid)) { br = rv; bid = int(j); }
     }
@@ -1508,7 +1527,7 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
     }
     // kSlow: the cluster finishes the row exactly, each CTA on its own slice
     cluster_exact<T, CL>(P, row, cluster, data, pen, gath, rs, use_pen, rpv, geo.cta_start, n_cta,
-                         ms.slow_int, ms.wb);
+                         ms.slow_int, ms.wb, (race_ok && !parity) ? gnz : nullptr, geo);
   }
   // do not leave while peers may still read this CTA's shared memory
   cluster.sync();
