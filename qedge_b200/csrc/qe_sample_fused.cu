@@ -840,7 +840,6 @@ __global__ void __launch_bounds__(Cfg<CL>::NT, CL == 16 ? 4 : 2) fused_kernel(Fu
         int u, p;
         item_of(geo, item, u, p);
         const Unit un = unit_of(geo, u);
-#pragma unroll
         // common case: both tiles complete, no penalty, Philox noise -- every
         // block holds 8 valid elements and needs no per-element checks
         const bool lean = !use_pen && !(parity && need_race) && (2 * p + 2) * kTile <= un.L;

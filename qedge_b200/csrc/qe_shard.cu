@@ -563,8 +563,7 @@ __global__ void __launch_bounds__(kNT) merge_kernel(KernelArgs a, int nshards, c
   __shared__ double wsum[kNW];
   __shared__ int wkc[kNW];
   __shared__ int s_nk;
-  __shared__ float s_xM, s_nM, s_Sf;
-  __shared__ double s_S;
+  __shared__ float s_nM, s_Sf;
   __shared__ int s_type, s_out, s_status;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.x, B = a.batch;
@@ -644,7 +643,7 @@ __global__ void __launch_bounds__(kNT) merge_kernel(KernelArgs a, int nshards, c
         rt.Sf = Sf;
       }
       s_type = type; s_out = out; s_status = status;
-      s_xM = xM; s_nM = nM; s_S = S; s_Sf = Sf;
+      s_nM = nM; s_Sf = Sf;
     }
   }
   __syncthreads();
