@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define QE_ABI_VERSION 1
+#define QE_ABI_VERSION 2
 
 /* element type of the logits rows */
 enum qe_dtype { QE_DTYPE_F32 = 0, QE_DTYPE_BF16 = 1, QE_DTYPE_F16 = 2 };
@@ -31,7 +31,9 @@ enum qe_dtype { QE_DTYPE_F32 = 0, QE_DTYPE_BF16 = 1, QE_DTYPE_F16 = 2 };
 /* qe_sample_args.flags */
 enum qe_flags {
   QE_FLAG_ALL_GREEDY = 1u, /* BatchSampler.forward(all_greedy=True) (sampler.py:28-29) */
-  QE_FLAG_USE_TOP_P = 2u   /* BatchSampler.forward(use_top_p=True)  (sampler.py:34-38) */
+  QE_FLAG_USE_TOP_P = 2u,  /* BatchSampler.forward(use_top_p=True)  (sampler.py:34-38) */
+  QE_FLAG_MULTI_KERNEL = 4u /* run the five-launch cross-check path instead of the default
+                               single streaming launch (no min_ps, out_kept, out_norm) */
 };
 
 /* status codes */
@@ -48,7 +50,8 @@ enum qe_row_status {
   QE_ROW_GREEDY = 1,       /* row sampled as greedy argmax (T <= 1e-5 or all_greedy) */
   QE_ROW_NONFINITE = 2,    /* probabilities not finite; greedy argmax returned */
   QE_ROW_GATHERED = 4,     /* diagnostic: finished from the gathered head of the row */
-  QE_ROW_SLOW = 8          /* diagnostic: finished by the single-CTA exact fallback */
+  QE_ROW_SLOW = 8,         /* diagnostic: finished by the exact (threshold + race) rounds */
+  QE_ROW_TIMEOUT = 16      /* a bounded wait on this row's data gave up; out_ids[row] = -1 */
 };
 
 typedef struct qe_sample_args {
@@ -61,21 +64,28 @@ typedef struct qe_sample_args {
   const float* temperatures;   /* [B] (sampler.py:25 `temperatures`; greedy iff <= 1e-5) */
   const float* top_ps;         /* [B] or NULL (sampler.py:26 `top_ps`) */
   const int32_t* top_ks;       /* [B] or NULL; <= 0 or >= V means off (batch.py:154-157) */
+  const float* min_ps;         /* [B] or NULL; drop ids with p < min_p * max p (batch.py:60, 158) */
   const float* rep_penalties;  /* [B] or NULL; repetition penalty over the history set */
   const int32_t* history;      /* [B, history_ld] token ids or NULL */
   const int32_t* history_lens; /* [B] valid entries per row, or NULL for all history_ld */
   int64_t history_ld;
   const float* noise;          /* [B, noise_ld] Exp(1) noise (parity mode) or NULL (Philox) */
   int64_t noise_ld;
-  uint64_t seed;               /* Philox key */
+  uint64_t seed;               /* Philox key of every row ... */
+  const uint64_t* seeds;       /* ... or [B] per-row keys (SamplingParams.seed), or NULL */
   uint64_t step;               /* Philox step (decode step) */
   const uint64_t* step_ptr;    /* device step counter; overrides `step` when non-NULL */
   int64_t row_offset;          /* global index of row 0 (keys the Philox stream) */
   uint32_t flags;              /* enum qe_flags */
+  uint32_t wait_polls;         /* 0: default bound on every device-side wait (about a second);
+                                  n > 0: give up after n - 1 polls (tests of the timeout path) */
   int64_t* out_ids;            /* [B] sampled token ids (int64, like torch.argmax) */
   float* out_probs;            /* [B, probs_ld] softmax probabilities or NULL */
   int64_t probs_ld;
   int32_t* out_status;         /* [B] enum qe_row_status bits or NULL */
+  int64_t* out_kept;           /* debug, [B] or NULL: size of the kept set (0 for greedy and
+                                  non-finite rows, V without filters); forces the exact rounds */
+  double* out_norm;            /* debug, [B] or NULL: sum_j exp((x_j - max x) / T) */
   void* workspace;             /* device scratch, >= qe_sample_workspace_size() bytes */
   size_t workspace_bytes;
 } qe_sample_args;
@@ -83,7 +93,8 @@ typedef struct qe_sample_args {
 /* ABI version of the loaded library (QE_ABI_VERSION). */
 int qe_abi_version(void);
 
-/* Bytes of device workspace qe_sample needs for a batch of B rows of V ids. */
+/* Bytes of device workspace qe_sample needs for a batch of B rows of V ids
+ * (enough for either path).  The library never needs it zeroed. */
 size_t qe_sample_workspace_size(int64_t batch, int64_t vocab);
 
 /* Sample one token per row on `stream` (a cudaStream_t; NULL = legacy default
@@ -93,6 +104,12 @@ int qe_sample(const qe_sample_args* args, void* stream);
 
 /* Message of the last error returned on this thread ("" if none). */
 const char* qe_last_error(void);
+
+/* Device-side error bits of the last qe_sample call that used `workspace`
+ * (1: a bounded wait gave up; its rows carry QE_ROW_TIMEOUT and id -1).
+ * Waits for `stream`, then copies one word to the host.  This is the only
+ * call of the library that synchronises the host. */
+int qe_sample_errors(const void* workspace, void* stream, uint32_t* flags);
 
 /* Bytes of the scratch array built into the library for qe_sample_noalloc. */
 #define QE_NOALLOC_SCRATCH_BYTES (32u << 20)

@@ -11,15 +11,15 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqesample.so"
 
-QE_ABI_VERSION = 1
+QE_ABI_VERSION = 2
 QE_DTYPE_F32, QE_DTYPE_BF16, QE_DTYPE_F16 = 0, 1, 2
-QE_FLAG_ALL_GREEDY, QE_FLAG_USE_TOP_P = 1, 2
-QE_ROW_GREEDY, QE_ROW_NONFINITE, QE_ROW_GATHERED, QE_ROW_SLOW = 1, 2, 4, 8
+QE_FLAG_ALL_GREEDY, QE_FLAG_USE_TOP_P, QE_FLAG_MULTI_KERNEL = 1, 2, 4
+QE_ROW_GREEDY, QE_ROW_NONFINITE, QE_ROW_GATHERED, QE_ROW_SLOW, QE_ROW_TIMEOUT = 1, 2, 4, 8, 16
 STATUS_NAMES = {0: "QE_OK", -1: "QE_ERR_INVALID", -2: "QE_ERR_CUDA",
                 -3: "QE_ERR_WORKSPACE", -4: "QE_ERR_UNSUPPORTED"}
 
 # Every symbol the header declares; tests check the library exports them.
-EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error",
+EXPORTED = ("qe_abi_version", "qe_sample_workspace_size", "qe_sample", "qe_last_error", "qe_sample_errors",
             "qe_sample_noalloc", "qe_shard_record_bytes", "qe_shard_test_bytes", "qe_shard_partial_bytes",
             "qe_shard_summarize", "qe_shard_merge", "qe_shard_test", "qe_shard_decide")
 QE_NOALLOC_SCRATCH_BYTES = 32 << 20
@@ -38,6 +38,7 @@ class QeSampleArgs(ctypes.Structure):
         ("temperatures", _vp),
         ("top_ps", _vp),
         ("top_ks", _vp),
+        ("min_ps", _vp),
         ("rep_penalties", _vp),
         ("history", _vp),
         ("history_lens", _vp),
@@ -45,14 +46,18 @@ class QeSampleArgs(ctypes.Structure):
         ("noise", _vp),
         ("noise_ld", ctypes.c_int64),
         ("seed", ctypes.c_uint64),
+        ("seeds", _vp),
         ("step", ctypes.c_uint64),
         ("step_ptr", _vp),
         ("row_offset", ctypes.c_int64),
         ("flags", ctypes.c_uint32),
+        ("wait_polls", ctypes.c_uint32),
         ("out_ids", _vp),
         ("out_probs", _vp),
         ("probs_ld", ctypes.c_int64),
         ("out_status", _vp),
+        ("out_kept", _vp),
+        ("out_norm", _vp),
         ("workspace", _vp),
         ("workspace_bytes", ctypes.c_size_t),
     ]
@@ -86,6 +91,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
         lib.qe_sample_noalloc.argtypes = [ctypes.POINTER(QeSampleArgs), _vp]
         lib.qe_last_error.restype = ctypes.c_char_p
         lib.qe_last_error.argtypes = []
+        lib.qe_sample_errors.restype = ctypes.c_int
+        lib.qe_sample_errors.argtypes = [_vp, _vp, ctypes.POINTER(ctypes.c_uint32)]
         for name in ("qe_shard_record_bytes", "qe_shard_test_bytes", "qe_shard_partial_bytes"):
             getattr(lib, name).restype = ctypes.c_size_t
             getattr(lib, name).argtypes = []

@@ -1,8 +1,7 @@
 // qe_abi.cu — the exported C ABI (include/qedge_sample.h): argument
-// validation, workspace layout and dispatch to the sampler kernels.
+// validation, workspace layout and dispatch to the sampler paths.
 #include <cuda_runtime.h>
 
-#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -26,6 +25,7 @@ int64_t groups_per_row(int64_t vocab) {
   return n;
 }
 
+// Scratch of the multi-kernel path (qe_sample_ref.cu).
 size_t workspace_bytes(int64_t batch, int64_t vocab) {
   size_t b = size_t(batch);
   size_t n = align_up(b * size_t(groups_per_row(vocab)) * sizeof(GroupPart), 256);
@@ -53,6 +53,16 @@ Workspace carve_workspace(void* base, int64_t batch, int64_t vocab) {
   return w;
 }
 
+// The multi-kernel path serves the debug probabilities and callers that ask
+// for it; everything else runs the streaming path.
+static bool uses_multi_kernel(const qe_sample_args* a) {
+  return a->out_probs != nullptr || (a->flags & QE_FLAG_MULTI_KERNEL) != 0u;
+}
+
+size_t call_workspace_bytes(const qe_sample_args* a) {
+  return uses_multi_kernel(a) ? workspace_bytes(a->batch, a->vocab) : stream_workspace_bytes(a->batch, a->vocab);
+}
+
 }  // namespace qe
 
 using namespace qe;
@@ -62,7 +72,19 @@ extern "C" int qe_abi_version(void) { return QE_ABI_VERSION; }
 extern "C" const char* qe_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" size_t qe_sample_workspace_size(int64_t batch, int64_t vocab) {
-  return batch > 0 && vocab > 0 ? workspace_bytes(batch, vocab) : 0;
+  if (batch <= 0 || vocab <= 0) return 0;
+  const size_t a = workspace_bytes(batch, vocab), b = stream_workspace_bytes(batch, vocab);
+  return a > b ? a : b;
+}
+
+extern "C" int qe_sample_errors(const void* workspace, void* stream, uint32_t* flags) {
+  g_last_error.clear();
+  if (!workspace || !flags) return set_error(QE_ERR_INVALID, "workspace and flags are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemcpy(flags, stream_error_word(workspace), sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("qe_sample_errors: ") + cudaGetErrorString(e));
+  return QE_OK;
 }
 
 extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
@@ -82,47 +104,44 @@ extern "C" int qe_sample(const qe_sample_args* a, void* stream) {
   if (a->noise && a->noise_ld < a->vocab) return set_error(QE_ERR_INVALID, "noise_ld < vocab");
   if (a->out_probs && a->probs_ld < a->vocab) return set_error(QE_ERR_INVALID, "probs_ld < vocab");
   if (a->history && a->history_ld < 0) return set_error(QE_ERR_INVALID, "history_ld < 0");
+  const bool multi = uses_multi_kernel(a);
+  if (multi && (a->min_ps || a->out_kept || a->out_norm))
+    return set_error(QE_ERR_UNSUPPORTED, "min_ps, out_kept and out_norm need the streaming path (no out_probs)");
   const bool pen = a->history && a->rep_penalties;
-  if (pen && a->vocab > 48 * 1024 * 32)
-    return set_error(QE_ERR_UNSUPPORTED, "repetition penalty supports vocab <= 1,572,864");
-  const size_t need = workspace_bytes(a->batch, a->vocab);
+  if (multi && pen && a->vocab > 48 * 1024 * 32)
+    return set_error(QE_ERR_UNSUPPORTED, "repetition penalty on the multi-kernel path supports vocab <= 1,572,864");
+  const size_t need = call_workspace_bytes(a);
   if (!a->workspace || a->workspace_bytes < need)
     return set_error(QE_ERR_WORKSPACE, "workspace smaller than qe_sample_workspace_size()");
   if (reinterpret_cast<uintptr_t>(a->workspace) % 256)
     return set_error(QE_ERR_INVALID, "workspace must be 256-byte aligned");
 
   KernelArgs ka;
+  std::memset(&ka, 0, sizeof(ka));
   ka.dtype = a->dtype;
   ka.batch = a->batch; ka.vocab = a->vocab; ka.ld = a->ld;
   ka.logits = a->logits;
   ka.temperatures = a->temperatures;
   ka.top_ps = a->top_ps;
   ka.top_ks = a->top_ks;
+  ka.min_ps = a->min_ps;
   ka.rep_penalties = a->rep_penalties;
   ka.history = pen ? a->history : nullptr;
   ka.history_lens = a->history_lens;
   ka.history_ld = a->history_ld;
   ka.noise = a->noise; ka.noise_ld = a->noise_ld;
-  ka.seed = a->seed; ka.step = a->step; ka.step_ptr = a->step_ptr;
+  ka.seed = a->seed; ka.seeds = a->seeds; ka.step = a->step; ka.step_ptr = a->step_ptr;
   ka.row_offset = a->row_offset;
   ka.flags = a->flags;
+  ka.wait_polls = a->wait_polls;
   ka.out_ids = a->out_ids;
   ka.out_probs = a->out_probs; ka.probs_ld = a->probs_ld;
   ka.out_status = a->out_status;
-  ka.ws = carve_workspace(a->workspace, a->batch, a->vocab);
+  ka.out_kept = a->out_kept;
+  ka.out_norm = a->out_norm;
+  ka.workspace = a->workspace;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // path choice: the fused cluster kernel unless QE_SAMPLER_PATH=ref, the
-  // debug probabilities are requested, or the vocabulary is too large
-  const char* env = std::getenv("QE_SAMPLER_PATH");
-  const int forced = (env && !std::strcmp(env, "ref")) ? 1 : (env && !std::strcmp(env, "fused")) ? 2 : 0;
-  // 8 CTAs x 512 threads per row (measured faster than 16 x 256 on B200 for
-  // every dtype); QE_FUSED_CLUSTER=16 selects the 16-CTA shape for 16-bit rows
-  int cluster = 8;
-  if (const char* cl = std::getenv("QE_FUSED_CLUSTER")) {
-    if (cl[0] == '1' && cl[1] == '6' && a->dtype != QE_DTYPE_F32) cluster = 16;
-  }
-  const bool fused_ok = !a->out_probs && fused_capacity(a->vocab, cluster) > 0;
-  if (forced != 1 && fused_ok) return launch_fused(ka, st, cluster);
-  if (forced == 2 && !fused_ok && !a->out_probs) return set_error(QE_ERR_UNSUPPORTED, "QE_SAMPLER_PATH=fused but the fused path cannot take this call");
+  if (!multi) return launch_stream(ka, st);
+  ka.ws = carve_workspace(a->workspace, a->batch, a->vocab);
   return launch_ref_path(ka, st);
 }

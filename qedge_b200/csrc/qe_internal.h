@@ -64,6 +64,7 @@ struct KernelArgs {
   const float* temperatures;
   const float* top_ps;
   const int32_t* top_ks;
+  const float* min_ps;
   const float* rep_penalties;
   const int32_t* history;
   const int32_t* history_lens;
@@ -71,15 +72,25 @@ struct KernelArgs {
   const float* noise;
   int64_t noise_ld;
   uint64_t seed, step;
+  const uint64_t* seeds;
   const uint64_t* step_ptr;
   int64_t row_offset;
   uint32_t flags;
+  uint32_t wait_polls;
   int64_t* out_ids;
   float* out_probs;
   int64_t probs_ld;
   int32_t* out_status;
+  int64_t* out_kept;
+  double* out_norm;
+  void* workspace;
   Workspace ws;
 };
+
+// Philox key of a row: the per-row seed when given, else the call's seed.
+__host__ __device__ inline uint64_t row_seed(const KernelArgs& a, int64_t row) {
+  return a.seeds ? a.seeds[row] : a.seed;
+}
 
 size_t workspace_bytes(int64_t batch, int64_t vocab);
 Workspace carve_workspace(void* base, int64_t batch, int64_t vocab);
@@ -87,7 +98,14 @@ int64_t groups_per_row(int64_t vocab);
 
 int set_error(int code, const std::string& msg);
 int launch_ref_path(const KernelArgs& ka, cudaStream_t st);
-int fused_capacity(int64_t V, int cluster);
-int launch_fused(const KernelArgs& ka, cudaStream_t st, int cluster);
+// Workspace bytes of the path qe_sample takes for these arguments.
+size_t call_workspace_bytes(const qe_sample_args* a);
+
+// The streaming sampler (qe_sample_stream.cu): the default path.
+bool stream_supports(int64_t vocab);
+size_t stream_workspace_bytes(int64_t batch, int64_t vocab);
+int launch_stream(const KernelArgs& ka, cudaStream_t st);
+// Device error word of the streaming path inside a workspace.
+const void* stream_error_word(const void* workspace);
 
 }  // namespace qe

@@ -57,7 +57,7 @@ extern "C" int qe_sample_noalloc(const qe_sample_args* a, void* stream) {
     return set_error(QE_ERR_INVALID, "struct_size mismatch (header/library version skew)");
   if (a->batch <= 0 || a->vocab < 1 || a->vocab >= (int64_t(1) << 24))
     return qe_sample(a, stream);  // qe_sample handles empty batches and reports bad sizes
-  const size_t need = qe_sample_workspace_size(a->batch, a->vocab);
+  const size_t need = call_workspace_bytes(a);
   if (need > kNoAllocBytes)
     return set_error(QE_ERR_UNSUPPORTED,
                      "qe_sample_noalloc: " + std::to_string(a->batch) + " rows of " + std::to_string(a->vocab) +

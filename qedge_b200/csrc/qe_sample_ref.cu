@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(256) race_kernel(KernelArgs a) {
   const long long tie_keep = ri->tie_keep;
   long long tie_base = ri->tie_prefix[g];
   const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
-  const NoiseKey key = make_noise_key(a.seed, step, a.row_offset + row);
+  const NoiseKey key = make_noise_key(row_seed(a, row), step, a.row_offset + row);
   NoiseRoot root{0.f, 0};
   int64_t gid_s = -1; int mem_s = 0;
   if (!a.noise) {

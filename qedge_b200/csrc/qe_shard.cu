@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kNT) summarize_kernel(KernelArgs a, int shard,
   int mem_s = 0;
   if (!parity && (race_ok || rp.small_k)) {
     const uint64_t step = a.step_ptr ? *a.step_ptr : a.step;
-    nkey = make_noise_key(a.seed, step, a.row_offset + row);
+    nkey = make_noise_key(row_seed(a, row), step, a.row_offset + row);
     rt = noise_root(nkey, V);
     token_group(rt.s, V, &gid_s, &mem_s);
   }
@@ -881,6 +881,8 @@ int shard_args(const qe_sample_args* a, int nshards, KernelArgs& ka) {
     return set_error(QE_ERR_INVALID, "unknown dtype");
   if (!a->temperatures || !a->out_ids) return set_error(QE_ERR_INVALID, "temperatures and out_ids are required");
   if (a->history && a->history_ld < 0) return set_error(QE_ERR_INVALID, "history_ld < 0");
+  if (a->min_ps || a->out_kept || a->out_norm || a->out_probs)
+    return set_error(QE_ERR_UNSUPPORTED, "sharded path: min_ps, out_kept, out_norm and out_probs are not supported");
   ka = KernelArgs{};
   ka.dtype = a->dtype;
   ka.batch = a->batch; ka.vocab = a->vocab; ka.ld = a->ld;
@@ -891,7 +893,7 @@ int shard_args(const qe_sample_args* a, int nshards, KernelArgs& ka) {
   ka.rep_penalties = a->rep_penalties;
   ka.history = a->history; ka.history_lens = a->history_lens; ka.history_ld = a->history_ld;
   ka.noise = a->noise; ka.noise_ld = a->noise_ld;
-  ka.seed = a->seed; ka.step = a->step; ka.step_ptr = a->step_ptr;
+  ka.seed = a->seed; ka.seeds = a->seeds; ka.step = a->step; ka.step_ptr = a->step_ptr;
   ka.row_offset = a->row_offset;
   ka.flags = a->flags;
   ka.out_ids = a->out_ids;

@@ -20,18 +20,12 @@ pytestmark = pytest.mark.gpu
 CASES = C.build_cases()
 
 
-@pytest.fixture(scope="module", params=["fused", "ref"])
+@pytest.fixture(scope="module", params=["stream", "multi"])
 def sampler(request):
-    """Both kernel paths: the fused cluster kernel and the multi-kernel one."""
-    import os
+    """Both kernel paths: the single streaming launch (default) and the
+    five-launch multi-kernel cross-check."""
     from qedge_b200.sampler import QESampler
-    old = os.environ.get("QE_SAMPLER_PATH")
-    os.environ["QE_SAMPLER_PATH"] = request.param
-    yield QESampler(seed=0)
-    if old is None:
-        os.environ.pop("QE_SAMPLER_PATH", None)
-    else:
-        os.environ["QE_SAMPLER_PATH"] = old
+    return QESampler(seed=0, path=request.param)
 
 
 @pytest.mark.parametrize("name", sorted(CASES))
@@ -166,11 +160,10 @@ def test_fallback_paths_vs_oracle(sampler):
     np.testing.assert_array_equal(ids, oracle_ids(w, noise))
 
 
-def test_vocab_beyond_fused_capacity_uses_multikernel_path(monkeypatch):
-    """V above the fused kernel's shared-memory capacity (262,144) is served
-    by the multi-kernel path under the default dispatch, with the same ids."""
+def test_vocab_beyond_one_buffer_per_slice(sampler):
+    """V = 300,001: canonical slices longer than one chunk buffer are split
+    over several chunks (streaming path); ids equal the oracle's."""
     from qedge_b200.sampler import QESampler
-    monkeypatch.delenv("QE_SAMPLER_PATH", raising=False)
     V, B = 300_001, 4
     g = np.random.Generator(np.random.PCG64(17))
     x = g.standard_normal((B, V), dtype=np.float32) * np.float32(2.0)
@@ -178,5 +171,5 @@ def test_vocab_beyond_fused_capacity_uses_multikernel_path(monkeypatch):
                    np.array([0.9, 0.9, 0.5, 1.0], np.float32), np.array([0, 0, 40, 0], np.int32),
                    np.ones(B, np.float32), None, None, use_top_p=True)
     noise = ON.philox_noise(B, V, 8, 2)
-    ids = run(QESampler(seed=8), w, None, seed=8, step=2)
+    ids = run(QESampler(seed=8, path=sampler.path), w, None, seed=8, step=2)
     np.testing.assert_array_equal(ids, oracle_ids(w, noise))

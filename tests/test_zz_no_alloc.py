@@ -38,7 +38,7 @@ def test_noalloc_exported_and_rejects_oversize_before_touching_the_gpu():
     assert lib.qe_sample_noalloc(None, None) == -1
 
 
-def _call(lib, fn, w, dev_tensors, out, step, ws=None):
+def _call(lib, fn, w, dev_tensors, out, step, ws=None, flags=0):
     import torch
     lg, temps, tps, tks, rps, hist, hlen = dev_tensors
     a = N.QeSampleArgs()
@@ -56,7 +56,7 @@ def _call(lib, fn, w, dev_tensors, out, step, ws=None):
         a.history_ld = hist.stride(0)
     a.seed = 31
     a.step = step
-    a.flags = N.QE_FLAG_USE_TOP_P if w.use_top_p else 0
+    a.flags = (N.QE_FLAG_USE_TOP_P if w.use_top_p else 0) | flags
     a.out_ids = out.data_ptr()
     if ws is not None:
         a.workspace = ws.data_ptr()
@@ -68,10 +68,10 @@ def _call(lib, fn, w, dev_tensors, out, step, ws=None):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("path", ["fused", "ref"])
-def test_noalloc_matches_workspace_entry_point_twice(path, monkeypatch):
+@pytest.mark.parametrize("path", ["stream", "multi"])
+def test_noalloc_matches_workspace_entry_point_twice(path):
     import torch
-    monkeypatch.setenv("QE_SAMPLER_PATH", path)
+    flags = N.QE_FLAG_MULTI_KERNEL if path == "multi" else 0
     lib = N.load()
     dev = torch.device("cuda", 0)
     for w in (W.config2(B=16), W.config3(B=8)):
@@ -83,6 +83,6 @@ def test_noalloc_matches_workspace_entry_point_twice(path, monkeypatch):
         ws = torch.zeros(lib.qe_sample_workspace_size(w.B, w.V), dtype=torch.uint8, device=dev)
         out = torch.empty(w.B, dtype=torch.int64, device=dev)
         for step in (0, 1):
-            want = _call(lib, lib.qe_sample, w, tensors, out, step, ws=ws)
-            got = _call(lib, lib.qe_sample_noalloc, w, tensors, out, step)
+            want = _call(lib, lib.qe_sample, w, tensors, out, step, ws=ws, flags=flags)
+            got = _call(lib, lib.qe_sample_noalloc, w, tensors, out, step, flags=flags)
             np.testing.assert_array_equal(got, want)
