@@ -67,6 +67,10 @@ __device__ __forceinline__ unsigned int ld_relaxed(const unsigned int* p) {
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Release/acquire fence at GPU scope, issued by one thread after a CTA
+// barrier: it orders the whole CTA's earlier writes (cumulativity through the
+// barrier) before that thread's next signal, and its later reads after it.
+__device__ __forceinline__ void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void st_release(unsigned int* p, unsigned int v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -116,21 +120,43 @@ struct Params {
   HistAcc* hacc;
 };
 
+// ---------------------------------------------------------------- row parameters
+struct RowP {
+  int kind;
+  bool p_on, k_on, m_on, filtered, pen, exact;
+  float T, c1, tp, minp, rp;
+  long long k;
+  const int32_t* hist;
+  int hlen;
+};
+
 // ---------------------------------------------------------------- shared memory
 struct Q2Ent {
   uint16_t lg;
   uint8_t arg, arg2;
-  float E2;
+  float E2;   // lower bound on the group's second smallest noise
 };
+constexpr int kFCap = 256;   // race finalists per chunk (overflow: conservative)
+constexpr int kFW = 64;      // race finalists per warp in the chunk pass (overflow: conservative)
 
 struct alignas(128) Smem {
   unsigned char buf[kNumBuf][kBufBytes];
   uint64_t full[kNumBuf];
   uint64_t empty[kNumBuf];
-  long long item[kNumBuf];      // >= 0: chunk item; <= -2: follow-up item (-2 - j); -1: end
-  int frow[kNumBuf];            // row of a follow-up item
+  // per buffer, written by the producer before it completes `full`
+  int kind[kNumBuf];            // ItemKind
+  int chunk[kNumBuf];           // chunk index of a chunk or follow-up item
+  int frow[kNumBuf];            // row of the item
   int bulk_elems[kNumBuf];      // elements delivered by the bulk copy
-  int fin;
+  RowP rowp[kNumBuf];           // the row's parameters
+  float root_e[kNumBuf];        // the row's noise-tree root (Philox mode)
+  long long root_gid[kNumBuf];
+  int root_mem[kNumBuf];
+  // per buffer, written by the compute warps before they release it: the row
+  // whose part they filed (-1: none); the producer turns it into an arrival
+  int mail[kNumBuf];
+  int finq[kFinQ];              // producer-private ring of rows to finish
+  long long bcast_pre;
   int nq1, nq2, nq3;
   int ngath, over;
   int red_greedy;
@@ -141,6 +167,8 @@ struct alignas(128) Smem {
   float cceil;
   int ncand;
   Cand cand[kR];
+  Cand tc[kTC];
+  int ntc;
   uint32_t pen[kMaxGroups];
   float gmax[kMaxGroups];
   uint32_t red_k[kWarps];
@@ -149,11 +177,20 @@ struct alignas(128) Smem {
   long long red_l[kWarps];
   Cand wl[kWarps][kR];
   float wceil[kWarps];
-  uint16_t q1[kMaxGroups];
   Q2Ent q2[kQ2Cap];
-  uint32_t q3[kQ3Cap];
+  uint16_t fq[kFCap];           // race finalists: type << 14 | local group << 5 | member
+  int nf;
+  float theta;
+  unsigned int ceil_bits;       // CTA ceiling (non-negative float bits, atomicMax)
+  float wtop[kWarps][kR];
+  // warp-local chunk pass: each warp's max (ordered key), exponent anchor,
+  // sum in its own scale, and finalists
+  uint32_t wr_key[kWarps];
+  float wr_u[kWarps];
+  double wr_S[kWarps];
+  uint16_t fqw[kWarps][kFW];
   uint32_t phist[kWarps][kBins];
-  float topm[kWarps][8];
+  float topm[kWarps][kTopM];
   GItem gl[kGCap];
   double pd[kWarps][kTC];
   long long pl[kWarps][kTC];
@@ -212,17 +249,7 @@ __device__ __forceinline__ int gsize(int len, int tile, int gl) {
   return n;
 }
 
-// ---------------------------------------------------------------- row parameters
-struct RowP {
-  int kind;
-  bool p_on, k_on, m_on, filtered, pen, exact;
-  float T, c1, tp, minp, rp;
-  long long k;
-  const int32_t* hist;
-  int hlen;
-};
-
-__device__ RowP row_params(const Params& P, int row) {
+__device__ __noinline__ RowP row_params(const Params& P, int row) {
   const KernelArgs& a = P.a;
   RowP r;
   const int64_t V = a.vocab;
@@ -318,7 +345,7 @@ __device__ void fill_chunk(const Params& P, unsigned char* buf, const Geo& g, in
 
 // Repetition-penalty bits of the chunk: bit m of pen[lg] marks member m of
 // local group lg as a history id.
-__device__ void build_pen(Smem& sm, const Geo& g, const RowP& rp) {
+__device__ __forceinline__ void build_pen(Smem& sm, const Geo& g, const RowP& rp) {
   for (int i = threadIdx.x; i < g.ntiles * 32; i += kThreads) sm.pen[i] = 0u;
   csync();
   for (int h = threadIdx.x; h < rp.hlen; h += kThreads) {
@@ -370,6 +397,28 @@ __device__ __forceinline__ float group_sum(const float* x, float c1, float c0) {
     s3 += qe_ex2_ftz(__fmaf_rn(x[m + 3], c1, c0));
   }
   return (s0 + s1) + (s2 + s3);
+}
+
+// A group holding history ids: unpack, penalise, reduce in fp32.
+template <typename T>
+__device__ __forceinline__ G1 pass1_pen(const unsigned char* buf, const RowP& rp, int tile, int lane, uint32_t pb,
+                                     bool sum) {
+  G1 g;
+  float x[32];
+#pragma unroll
+  for (int m = 0; m < 32; ++m) {
+    float v = Elt<T>::at(buf, moff(tile, lane, m));
+    if ((pb >> m) & 1u) v = penalise(v, rp.rp);
+    x[m] = v;
+  }
+  float mx = x[0];
+#pragma unroll
+  for (int m = 1; m < 32; ++m) mx = fmax_nan(mx, x[m]);
+  g.gmax = mx;
+  g.fsum = 0.f;
+  if (!sum || !(g.gmax > -INFINITY)) return g;
+  g.fsum = group_sum(x, rp.c1, -__fmul_rn(g.gmax, rp.c1));
+  return g;
 }
 
 // Group max (NaN-propagating) and, when `sum`, the group-relative sum
@@ -429,21 +478,7 @@ __device__ __forceinline__ G1 pass1(const Smem& sm, const unsigned char* buf, co
       return g;
     }
   }
-  // a group holding history ids: unpack, penalise, reduce in fp32
-#pragma unroll
-  for (int m = 0; m < 32; ++m) {
-    float v = Elt<T>::at(buf, moff(tile, lane, m));
-    if ((pb >> m) & 1u) v = penalise(v, rp.rp);
-    x[m] = v;
-  }
-  float mx = x[0];
-#pragma unroll
-  for (int m = 1; m < 32; ++m) mx = fmax_nan(mx, x[m]);
-  g.gmax = mx;
-  g.fsum = 0.f;
-  if (!sum || !(g.gmax > -INFINITY)) return g;
-  g.fsum = group_sum(x, rp.c1, -__fmul_rn(g.gmax, rp.c1));
-  return g;
+  return pass1_pen<T>(buf, rp, tile, lane, pb, sum);
 }
 
 // ---------------------------------------------------------------- warp helpers
@@ -452,7 +487,7 @@ __device__ __forceinline__ uint32_t nan_key(float v) { return ordered_key(v); } 
 // Offer each lane's candidate (r >= 0; r < 0: none) to the warp's list wl of
 // R entries in race order (r desc, id asc).  Whatever does not stay in the
 // list raises the warp's ceiling.
-__device__ void warp_offer(Cand* wl, float* wceil, int R, float r, float x, float E, int id) {
+__device__ __forceinline__ void warp_offer(Cand* wl, float* wceil, int R, float r, float x, float E, int id) {
   const int lane = threadIdx.x & 31;
   uint32_t kr = r >= 0.f ? __float_as_uint(r) + 1u : 0u;
   float ceil = 0.f;
@@ -515,7 +550,7 @@ __device__ __forceinline__ float cta_theta(const Smem& sm, int R) {
 
 // Merge the warp lists into the CTA's R best (sm.cand, sm.ncand) and the
 // ceiling over every other token (sm.cceil).  Warp 0 only.
-__device__ void merge_lists(Smem& sm, int R) {
+__device__ __forceinline__ void merge_lists(Smem& sm, int R) {
   if ((threadIdx.x >> 5) != 0) return;
   const int lane = threadIdx.x & 31;
   Cand c{-1.f, 0.f, 1.f, INT_MAX};
@@ -568,32 +603,38 @@ struct Keep {
 };
 
 // ---------------------------------------------------------------- exact group noise
+// Out-of-line copies of the noise arithmetic: they run for a few groups and
+// tokens per chunk, and inlining them at every call site multiplies the
+// kernel's code size (instruction-cache misses cost more than the calls).
+__device__ __noinline__ U4 philox_nl(const NoiseKey& key, uint32_t index, uint32_t tag) {
+  return philox_at(key, index, tag);
+}
+__device__ __noinline__ float neglog_nl(float u) { return neglog(u); }
+__device__ __noinline__ float div_nl(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __noinline__ double exp2_nl(double d) { return exp2(d); }
 __device__ __forceinline__ float emin_exact(const U4& w, int n, bool holds, float e_root) {
   if (holds) return e_root;
-  const float l = neglog(uniform_open(w.x));
-  return __fadd_rn(e_root, n == 32 ? __fmul_rn(l, 0.03125f) : __fdiv_rn(l, float(n)));
+  const float l = neglog_nl(uniform_open(w.x));
+  return __fadd_rn(e_root, n == 32 ? __fmul_rn(l, 0.03125f) : div_nl(l, float(n)));
 }
 __device__ __forceinline__ int arg_of(const U4& w, int n, bool holds, int s_mem) {
   return holds ? s_mem : int(select_index32(w.y, uint32_t(n)));
 }
 __device__ __forceinline__ float e2_exact(const U4& w, int n, float emin) {
-  return __fadd_rn(emin, __fdiv_rn(neglog(uniform_open(w.z)), float(n - 1)));
+  return __fadd_rn(emin, div_nl(neglog_nl(uniform_open(w.z)), float(n - 1)));
 }
 __device__ __forceinline__ int arg2_of(const U4& w, int n, int arg) {
   const int i2 = int(select_index32(w.w, uint32_t(n - 1)));
   return i2 < arg ? i2 : i2 + 1;
 }
 
-// Root of the row's noise tree into shared memory (thread 0).
-__device__ void set_root(const Params& P, Smem& sm, int row) {
-  const NoiseKey key = row_key(P, row);
-  const NoiseRoot rt = noise_root(key, P.a.vocab);
-  int64_t gs = -1;
-  int ms = 0;
-  token_group(rt.s, P.a.vocab, &gs, &ms);
-  sm.e_root = rt.e_root;
-  sm.s_gid = gs;
-  sm.s_mem = ms;
+// Global group id and member index of token j (the slice table of the launch).
+__device__ __forceinline__ void token_group_p(const Params& P, int64_t j, int64_t* gid, int* mem) {
+  int sl = 0;
+  while (sl + 1 < kNumSlices && P.sstart[sl + 1] <= j) ++sl;
+  const int64_t o = j - P.sstart[sl];
+  *gid = P.gbase[sl] + local_group(o);
+  *mem = member_index(o);
 }
 
 // The kTC best (rho desc, id asc) that one thread has seen.
@@ -630,212 +671,218 @@ struct Top4 {
 };
 
 // ---------------------------------------------------------------- race: Philox noise tree
-// Lazy race over the chunk in the scale c0s: leaves the R best (ratio
-// e/E, with e = 2^(x c1 + c0s)) in sm.cand and a ceiling over every other
-// (kept) token in sm.cceil.  Every bound carries a relative margin >= 1e-5 on
-// top of the few-ulp rounding of the quantities it bounds.
+// Bounds first, exact noise last.  Every group gets one Philox call; its two
+// smallest noises are bracketed with the hardware log (lg2.approx, whose
+// error is far inside the 3e-5 relative + 3e-5 absolute margin used here),
+// giving lower and upper bounds on the ratios of its noise-minimum and
+// second-minimum members and an upper bound on all its other members.  The
+// R-th largest lower bound is a valid threshold; whatever can still reach it
+// becomes a finalist and only finalists get the exact noise of the tree
+// (oracle-identical IEEE arithmetic).  Everything else feeds the ceiling.
+enum : int { kFinA = 0, kFinB = 1, kFinT = 2 };
+
+// Exact noise of a finalist (noise minimum, second minimum or another member
+// m of the group with global id gid and n members); *mem gets the member.
+// Out of line with scalar arguments only.
+__device__ __noinline__ float finalist_noise(NoiseKey key, long long gid, int n, long long s_gid, int s_mem,
+                                             float e_root, int type, int m, long long j, int* mem) {
+  const U4 w = philox_at(key, uint32_t(gid), kTagGroup);
+  const bool holds = gid == s_gid;
+  const int arg = arg_of(w, n, holds, s_mem);
+  const float emin = emin_exact(w, n, holds, e_root);
+  *mem = arg;
+  if (type == kFinA) return emin;
+  const float e2 = e2_exact(w, n, emin);
+  if (type == kFinB) {
+    *mem = arg2_of(w, n, arg);
+    return e2;
+  }
+  *mem = m;
+  const U4 wt = philox_at(key, uint32_t(j >> 2), kTagToken);
+  const uint32_t word = (j & 3) == 0 ? wt.x : (j & 3) == 1 ? wt.y : (j & 3) == 2 ? wt.z : wt.w;
+  return __fadd_rn(e2, neglog(uniform_open(word)));
+}
+
+// Exact candidate for a finalist.
 template <typename T>
-__device__ void race_philox(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp,
-                            float c0s, int R, const Keep& keep) {
+__device__ __forceinline__ Cand finalist(const Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp,
+                                         const NoiseKey& key, float c0s, uint32_t code) {
+  const int type = int(code >> 14), lg = int((code >> 5) & 0x1FFu), m = int(code & 31u);
+  const int tile = lg >> 5, gl = lg & 31;
+  int mem = 0;
+  const float E = finalist_noise(key, g.gbase + lg, gsize(g.len, tile, gl), sm.s_gid, sm.s_mem, sm.e_root, type, m,
+                                 g.start + moff(tile, gl, m), &mem);
+  const float x = xval<T>(sm, buf, rp, tile, gl, mem);
+  return Cand{div_nl(qe_ex2_ftz(__fmaf_rn(x, rp.c1, c0s)), E), x, E, int(g.start + moff(tile, gl, mem))};
+}
+
+__device__ __forceinline__ void push_finalist(Smem& sm, uint32_t code, float hi, float& lc) {
+  const int f = atomicAdd(&sm.nf, 1);
+  if (f < kFCap) sm.fq[f] = uint16_t(code);
+  else lc = fmaxf(lc, hi);   // not evaluated: the ceiling keeps the record honest
+}
+
+// Race over the chunk in the scale c0s: leaves the R best (ratio e/E, with
+// e = 2^(x c1 + c0s)) in sm.cand and a ceiling over every other (kept) token
+// in sm.cceil.
+template <typename T>
+__device__ __forceinline__ void race_philox(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g,
+                                         const RowP& rp, float c0s, int R, const Keep& keep) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float c1 = rp.c1;
   const NoiseKey key = row_key(P, g.row);
-  const float e_root = sm.e_root;
+  const float c1 = rp.c1, e_root = sm.e_root;
   const long long s_gid = sm.s_gid;
   const int s_mem = sm.s_mem;
   if (lane == 0) {
     for (int i = 0; i < R; ++i) sm.wl[warp][i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
     sm.wceil[warp] = 0.f;
   }
-  if (tid == 0) sm.nq1 = sm.nq2 = sm.nq3 = 0;
-  csync();
-
-  // A: per group, a cheap upper bound on its best ratio and an approximate
-  // ratio of its noise-minimum member (seeds the threshold)
-  float ba[2] = {-1.f, -1.f}, ra[2] = {-1.f, -1.f};
-  bool sv[2] = {false, false};
+  if (tid == 0) {
+    sm.nq2 = 0;
+    sm.nf = 0;
+    sm.ceil_bits = 0u;
+  }
+  // A: bounds for the lane's two groups
+  float alo[2], ahi[2], blo[2], bhi[2], ob[2], el2[2];
+  int ag[2], ag2[2];
 #pragma unroll
   for (int s = 0; s < 2; ++s) {
+    alo[s] = ahi[s] = blo[s] = bhi[s] = ob[s] = -1.f;
+    el2[s] = 1.f;
+    ag[s] = ag2[s] = 0;
     const int tile = warp + kWarps * s;
     if (tile >= g.ntiles) continue;
     const int lg = tile * 32 + lane;
     const float gm = sm.gmax[lg];
     const int n = gsize(g.len, tile, lane);
     if (n <= 0 || !(gm > -INFINITY) || !keep.group_may(gm)) continue;
-    sv[s] = true;
     const long long gid = g.gbase + lg;
     const U4 w = philox_at(key, uint32_t(gid), kTagGroup);
     const bool holds = gid == s_gid;
-    const int arg = arg_of(w, n, holds, s_mem);
-    float elo = e_root;
+    const int a = arg_of(w, n, holds, s_mem);
+    float lo1 = e_root, hi1 = e_root;
     if (!holds) {
       const float la = -lg2_approx(uniform_open(w.x)) * 0.6931472f;
-      elo = e_root + fmaxf(0.f, la * (1.f - 3e-5f) - 3e-5f) * (1.f / float(n)) * (1.f - 1e-6f);
+      const float inv = 1.f / float(n);
+      lo1 = (e_root + fmaxf(0.f, la * (1.f - 3e-5f) - 3e-5f) * inv) * (1.f - 2e-6f);
+      hi1 = (e_root + (la * (1.f + 3e-5f) + 3e-5f) * inv) * (1.f + 2e-6f);
     }
-    const float egm = qe_ex2_ftz(__fmaf_rn(gm, c1, c0s));
-    ba[s] = __fdividef(egm, elo) * (1.f + 1e-5f);
-    const float xa = xval<T>(sm, buf, rp, tile, lane, arg);
-    if (keep(sm, xa, moff(tile, lane, arg))) ra[s] = __fdividef(qe_ex2_ftz(__fmaf_rn(xa, c1, c0s)), elo);
+    ag[s] = a;
+    const float xa = xval<T>(sm, buf, rp, tile, lane, a);
+    if (keep(sm, xa, moff(tile, lane, a))) {
+      const float ea = qe_ex2_ftz(__fmaf_rn(xa, c1, c0s));
+      alo[s] = __fdividef(ea, hi1) * (1.f - 1e-5f);
+      ahi[s] = __fdividef(ea, lo1) * (1.f + 1e-5f);
+    }
+    if (n >= 2) {
+      const float lz = -lg2_approx(uniform_open(w.z)) * 0.6931472f;
+      const float inv1 = 1.f / float(n - 1);
+      const float lo2 = (lo1 + fmaxf(0.f, lz * (1.f - 3e-5f) - 3e-5f) * inv1) * (1.f - 2e-6f);
+      const float hi2 = (hi1 + (lz * (1.f + 3e-5f) + 3e-5f) * inv1) * (1.f + 2e-6f);
+      const int a2 = arg2_of(w, n, a);
+      ag2[s] = a2;
+      el2[s] = lo2;
+      const float xb = xval<T>(sm, buf, rp, tile, lane, a2);
+      if (keep(sm, xb, moff(tile, lane, a2))) {
+        const float eb = qe_ex2_ftz(__fmaf_rn(xb, c1, c0s));
+        blo[s] = __fdividef(eb, hi2) * (1.f - 1e-5f);
+        bhi[s] = __fdividef(eb, lo2) * (1.f + 1e-5f);
+      }
+      if (n >= 3) ob[s] = __fdividef(qe_ex2_ftz(__fmaf_rn(gm, c1, c0s)), lo2) * (1.f + 1e-5f);
+    }
   }
-  // seeds: the warp's R best approximate argmin ratios, made exact
-  for (int round = 0; round < R; ++round) {
-    const float mine = fmaxf(ra[0], ra[1]);
-    const uint32_t kk = mine >= 0.f ? __float_as_uint(mine) + 1u : 0u;
-    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kk);
-    if (km == 0u) break;
-    const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kk == km)) - 1;
-    float r = -1.f, x = 0.f, E = 1.f;
-    int id = INT_MAX;
-    if (lane == src) {
-      const int s = ra[0] >= ra[1] ? 0 : 1;
-      if (s == 0) ra[0] = -2.f;   // seeded: its argmin member is offered here
-      else ra[1] = -2.f;
-      const int tile = warp + kWarps * s, lg = tile * 32 + lane;
-      const int n = gsize(g.len, tile, lane);
-      const long long gid = g.gbase + lg;
-      const U4 w = philox_at(key, uint32_t(gid), kTagGroup);
-      const bool holds = gid == s_gid;
-      const int arg = arg_of(w, n, holds, s_mem);
-      E = emin_exact(w, n, holds, e_root);
-      x = xval<T>(sm, buf, rp, tile, lane, arg);
-      r = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(x, c1, c0s)), E);
-      id = int(g.start + moff(tile, lane, arg));
+  // the warp's R largest lower bounds
+  {
+    float v0 = alo[0], v1 = blo[0], v2 = alo[1], v3 = blo[1];
+    for (int round = 0; round < R; ++round) {
+      const float m = fmaxf(fmaxf(v0, v1), fmaxf(v2, v3));
+      const float wm = warp_max(m);
+      if (lane == 0) sm.wtop[warp][round] = wm;
+      const unsigned bal = __ballot_sync(0xFFFFFFFFu, m == wm);
+      if (lane == __ffs(bal) - 1) {
+        if (v0 == wm) v0 = -1.f;
+        else if (v1 == wm) v1 = -1.f;
+        else if (v2 == wm) v2 = -1.f;
+        else v3 = -1.f;
+      }
     }
-    warp_offer(sm.wl[warp], &sm.wceil[warp], R, r, x, E, id);
   }
   csync();
-
-  // B: groups whose bound reaches the threshold go to Q1
-  float theta = cta_theta(sm, R);
+  // threshold: the R-th largest lower bound of the CTA (a valid lower bound
+  // on the chunk's R-th best ratio)
+  if (warp == 0) {
+    const int nv = kWarps * R;
+    const float a = lane < nv ? sm.wtop[lane / R][lane % R] : -2.f;
+    int rank = 0;
+    for (int j = 0; j < nv; ++j) {
+      const float bj = __shfl_sync(0xFFFFFFFFu, a, j);
+      rank += int(bj > a || (bj == a && j < lane));
+    }
+    if (lane < nv && rank == R - 1) sm.theta = a;
+  }
+  csync();
+  const float theta = sm.theta;
+  // B: what can still reach the threshold becomes a finalist or an expansion
   float lc = 0.f;
 #pragma unroll
   for (int s = 0; s < 2; ++s) {
-    if (!sv[s]) continue;
     const int lg = (warp + kWarps * s) * 32 + lane;
-    if (ba[s] >= theta) {
-      const int q = atomicAdd(&sm.nq1, 1);
-      sm.q1[q] = uint16_t(lg | (ra[s] == -2.f ? 0x8000 : 0));
-    } else {
-      lc = fmaxf(lc, ba[s]);
+    if (ahi[s] >= 0.f) {
+      if (ahi[s] >= theta) push_finalist(sm, uint32_t(kFinA << 14) | uint32_t(lg << 5), ahi[s], lc);
+      else lc = fmaxf(lc, ahi[s]);
     }
-  }
-  raise_ceiling(sm, lc);
-  csync();
-
-  // C: exact noise minimum and second minimum of the Q1 groups; their two
-  // members are candidates, the rest is bounded through E2
-  theta = cta_theta(sm, R);
-  const int nq1 = sm.nq1;
-  for (int base = 0; base < nq1; base += kThreads) {
-    const int e = base + tid;
-    float rA = -1.f, xA = 0.f, EA = 1.f, rB = -1.f, xB = 0.f, EB = 1.f;
-    int idA = INT_MAX, idB = INT_MAX;
-    lc = 0.f;
-    if (e < nq1) {
-      const uint16_t q = sm.q1[e];
-      const int lg = q & 0x1FF, tile = lg >> 5, gl = lg & 31;
-      const bool seeded = (q & 0x8000) != 0;
-      const int n = gsize(g.len, tile, gl);
-      const long long gid = g.gbase + lg;
-      const U4 w = philox_at(key, uint32_t(gid), kTagGroup);
-      const bool holds = gid == s_gid;
-      const int arg = arg_of(w, n, holds, s_mem);
-      const float emin = emin_exact(w, n, holds, e_root);
-      if (!seeded) {
-        const float xa = xval<T>(sm, buf, rp, tile, gl, arg);
-        const int oa = moff(tile, gl, arg);
-        if (keep(sm, xa, oa)) {
-          rA = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xa, c1, c0s)), emin);
-          xA = xa;
-          EA = emin;
-          idA = int(g.start + oa);
-        }
-      }
-      if (n >= 2) {
-        const float e2 = e2_exact(w, n, emin);
-        const int arg2 = arg2_of(w, n, arg);
-        const float xb = xval<T>(sm, buf, rp, tile, gl, arg2);
-        const int ob = moff(tile, gl, arg2);
-        if (keep(sm, xb, ob)) {
-          rB = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xb, c1, c0s)), e2);
-          xB = xb;
-          EB = e2;
-          idB = int(g.start + ob);
-        }
-        if (n >= 3) {
-          const float egm = qe_ex2_ftz(__fmaf_rn(sm.gmax[lg], c1, c0s));
-          const float b2 = __fdividef(egm, e2) * (1.f + 1e-5f);
-          if (b2 >= theta) {
-            const int q2 = atomicAdd(&sm.nq2, 1);
-            if (q2 < kQ2Cap) sm.q2[q2] = Q2Ent{uint16_t(lg), uint8_t(arg), uint8_t(arg2), e2};
-            else lc = fmaxf(lc, b2);   // not expanded: the ceiling keeps the record honest
-          } else {
-            lc = fmaxf(lc, b2);
-          }
-        }
+    if (bhi[s] >= 0.f) {
+      if (bhi[s] >= theta) push_finalist(sm, uint32_t(kFinB << 14) | uint32_t(lg << 5), bhi[s], lc);
+      else lc = fmaxf(lc, bhi[s]);
+    }
+    if (ob[s] >= 0.f) {
+      if (ob[s] >= theta) {
+        const int q = atomicAdd(&sm.nq2, 1);
+        if (q < kQ2Cap) sm.q2[q] = Q2Ent{uint16_t(lg), uint8_t(ag[s]), uint8_t(ag2[s]), el2[s]};
+        else lc = fmaxf(lc, ob[s]);
+      } else {
+        lc = fmaxf(lc, ob[s]);
       }
     }
-    warp_offer(sm.wl[warp], &sm.wceil[warp], R, rA, xA, EA, idA);
-    warp_offer(sm.wl[warp], &sm.wceil[warp], R, rB, xB, EB, idB);
-    raise_ceiling(sm, lc);
   }
   csync();
-
-  // D: members of the Q2 groups whose bound e/E2 reaches the threshold go to Q3
-  theta = cta_theta(sm, R);
+  // C: members of expanded groups whose bound reaches the threshold
   const int nq2 = min(sm.nq2, kQ2Cap);
+#pragma unroll 1
   for (int e = warp; e < nq2; e += kWarps) {
     const Q2Ent q = sm.q2[e];
     const int tile = q.lg >> 5, gl = q.lg & 31;
     const int n = gsize(g.len, tile, gl);
     const int m = lane;
-    lc = 0.f;
     if (m < n && m != q.arg && m != q.arg2) {
       const float xm = xval<T>(sm, buf, rp, tile, gl, m);
       if (keep(sm, xm, moff(tile, gl, m))) {
         const float bm = __fdividef(qe_ex2_ftz(__fmaf_rn(xm, c1, c0s)), q.E2) * (1.f + 1e-5f);
-        if (bm >= theta) {
-          const int t = atomicAdd(&sm.nq3, 1);
-          if (t < kQ3Cap) sm.q3[t] = (uint32_t(e) << 5) | uint32_t(m);
-          else lc = fmaxf(lc, bm);
-        } else {
-          lc = fmaxf(lc, bm);
-        }
+        if (bm >= theta) push_finalist(sm, uint32_t(kFinT << 14) | uint32_t(q.lg << 5) | uint32_t(m), bm, lc);
+        else lc = fmaxf(lc, bm);
       }
     }
-    raise_ceiling(sm, lc);
   }
+  lc = warp_max(lc);
+  if (lane == 0 && lc > 0.f) atomicMax(&sm.ceil_bits, __float_as_uint(lc));
   csync();
-
-  // E: exact token noise of the Q3 members
-  const int nq3 = min(sm.nq3, kQ3Cap);
-  for (int base = 0; base < nq3; base += kThreads) {
+  // D: exact noise for the finalists, ranked in the warp lists
+  const int nf = min(sm.nf, kFCap);
+  for (int base = 0; base < nf; base += kThreads) {
     const int e = base + tid;
-    float r = -1.f, x = 0.f, E = 1.f;
-    int id = INT_MAX;
-    if (e < nq3) {
-      const uint32_t t = sm.q3[e];
-      const Q2Ent q = sm.q2[t >> 5];
-      const int m = int(t & 31u), tile = q.lg >> 5, gl = q.lg & 31;
-      const int om = moff(tile, gl, m);
-      const int64_t j = g.start + om;
-      const U4 w = philox_at(key, uint32_t(j >> 2), kTagToken);
-      const uint32_t word = (j & 3) == 0 ? w.x : (j & 3) == 1 ? w.y : (j & 3) == 2 ? w.z : w.w;
-      E = __fadd_rn(q.E2, neglog(uniform_open(word)));
-      x = xval<T>(sm, buf, rp, tile, gl, m);
-      r = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(x, c1, c0s)), E);
-      id = int(j);
-    }
-    warp_offer(sm.wl[warp], &sm.wceil[warp], R, r, x, E, id);
+    Cand c{-1.f, 0.f, 1.f, INT_MAX};
+    if (e < nf) c = finalist<T>(sm, buf, g, rp, key, c0s, sm.fq[e]);
+    warp_offer(sm.wl[warp], &sm.wceil[warp], R, c.r, c.x, c.E, c.id);
   }
   csync();
   merge_lists(sm, R);
+  if (tid == 0) sm.cceil = fmaxf(sm.cceil, __uint_as_float(sm.ceil_bits));
   csync();
 }
 
 // ---------------------------------------------------------------- race: caller noise (parity mode)
 template <typename T>
-__device__ void race_noise(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp,
+__device__ __forceinline__ void race_noise(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp,
                            float c0s, int R, const Keep& keep) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float c1 = rp.c1;
@@ -921,7 +968,7 @@ __device__ void chunk_pass1(Smem& sm, const unsigned char* buf, const Geo& g, co
 
 // First id of the chunk whose value is cmax (the first NaN when cmax is NaN).
 template <typename T>
-__device__ int chunk_greedy(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, const G1 sl[2],
+__device__ __noinline__ int chunk_greedy(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, const G1 sl[2],
                             float cmax) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool cnan = cmax != cmax;
@@ -977,15 +1024,15 @@ __device__ long long cta_sum_l(Smem& sm, long long v) {
 // ---------------------------------------------------------------- small top-k gather
 // Files every token of the chunk at or above lk, a lower bound on the
 // chunk's k-th largest (penalised) logit: the k-th largest among each warp's
-// ceil(k/8) largest group maxima.
+// kTopM largest group maxima (k group maxima, hence k tokens, reach it).
 template <typename T>
-__device__ void gather_head(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, const G1 sl[2]) {
+__device__ __forceinline__ void gather_head(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, const G1 sl[2]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = int(rp.k);
-  const int mw = (k + kWarps - 1) / kWarps;
   float v0 = warp < g.ntiles ? sl[0].gmax : -INFINITY;
   float v1 = warp + kWarps < g.ntiles ? sl[1].gmax : -INFINITY;
-  for (int i = 0; i < mw; ++i) {
+#pragma unroll 1
+  for (int i = 0; i < kTopM; ++i) {
     const float b = fmaxf(v0, v1);
     const uint32_t kb = ordered_key(b);
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kb);
@@ -996,26 +1043,22 @@ __device__ void gather_head(Smem& sm, const unsigned char* buf, const Geo& g, co
       else v1 = -INFINITY;
     }
   }
-  if (lane == 0)
-    for (int i = mw; i < 8; ++i) sm.topm[warp][i] = -INFINITY;
   if (tid == 0) {
     sm.ngath = 0;
     sm.over = 0;
+    sm.lk = -INFINITY;
   }
   csync();
-  if (warp == 0) {
-    const float a0 = sm.topm[lane >> 3][lane & 7], a1 = sm.topm[4 + (lane >> 3)][lane & 7];
-    int r0 = 0, r1 = 0;
-    for (int j = 0; j < 32; ++j) {
-      const float b0 = __shfl_sync(0xFFFFFFFFu, a0, j), b1 = __shfl_sync(0xFFFFFFFFu, a1, j);
-      r0 += int(b0 > a0 || (b0 == a0 && j < lane)) + int(b1 > a0);
-      r1 += int(b0 >= a1) + int(b1 > a1 || (b1 == a1 && j < lane));
+  if (tid < kWarps * kTopM) {
+    const float* tv = &sm.topm[0][0];
+    const float a = tv[tid];
+    int r = 0;
+#pragma unroll 1
+    for (int j = 0; j < kWarps * kTopM; ++j) {
+      const float b = tv[j];
+      r += int(b > a || (b == a && j < tid));
     }
-    const unsigned h0 = __ballot_sync(0xFFFFFFFFu, r0 == k - 1), h1 = __ballot_sync(0xFFFFFFFFu, r1 == k - 1);
-    float lk = -INFINITY;
-    if (h0) lk = __shfl_sync(0xFFFFFFFFu, a0, __ffs(h0) - 1);
-    else if (h1) lk = __shfl_sync(0xFFFFFFFFu, a1, __ffs(h1) - 1);
-    if (lane == 0) sm.lk = lk;
+    if (r == k - 1) sm.lk = a;
   }
   csync();
   const float lk = sm.lk;
@@ -1037,22 +1080,23 @@ __device__ void gather_head(Smem& sm, const unsigned char* buf, const Geo& g, co
 }
 
 // ---------------------------------------------------------------- row completion
-__device__ void complete_row(const Params& P, int row, long long id, int status, long long kept) {
+__device__ __noinline__ void complete_row(const Params& P, int row, long long id, int status, long long kept) {
   if (threadIdx.x != 0) return;
   const KernelArgs& a = P.a;
   a.out_ids[row] = id;
   if (a.out_status) a.out_status[row] = status;
   if (a.out_kept) a.out_kept[row] = kept;
-  __threadfence();
+  fence_acq_rel();
   atomicAdd(&P.ctl->rows_done, 1u);
 }
 
 // Publish the round in sm.rr for `row` (thread 0; callers csync before).
-__device__ void publish(const Params& P, Smem& sm, int row) {
+__device__ __forceinline__ void publish(const Params& P, Smem& sm, int row) {
   if (threadIdx.x != 0) return;
   P.round[row] = sm.rr;
   P.rowctl[row].cnt = 0u;
-  __threadfence();
+  P.rowctl[row].round = unsigned(sm.rr.type);
+  fence_acq_rel();
   const unsigned e = atomicAdd(&P.ctl->qentries, 1u);
   if (e < unsigned(P.a.batch) * kMaxRounds) {
     st_release(&P.queue[e], unsigned(row) + 1u);
@@ -1061,21 +1105,6 @@ __device__ void publish(const Params& P, Smem& sm, int row) {
     atomicOr(&P.ctl->err, 2u);
     complete_row(P, row, -1, QE_ROW_TIMEOUT, 0);
   }
-}
-
-// File this CTA's part of the row's current round; returns true in the CTA
-// that filed the last part (it then finishes the round).
-__device__ bool arrive(const Params& P, Smem& sm, int row) {
-  __threadfence();
-  csync();
-  if (threadIdx.x == 0) {
-    const unsigned old = atomicAdd(&P.rowctl[row].cnt, 1u);
-    const int last = old == unsigned(P.nc - 1);
-    if (last) __threadfence();
-    sm.fin = last;
-  }
-  csync();
-  return sm.fin != 0;
 }
 
 __device__ __forceinline__ int final_level(const Params& P, const RowP& rp) {
@@ -1089,7 +1118,7 @@ __device__ __forceinline__ float minp_threshold(const RowP& rp, float xmax, floa
 }
 
 // Start the exact rounds for a row whose candidates could not decide it.
-__device__ void enter_exact(const Params& P, Smem& sm, int row, const RowP& rp, float c0, float Sf, double S,
+__device__ __forceinline__ void enter_exact(const Params& P, Smem& sm, int row, const RowP& rp, float c0, float Sf, double S,
                             float thr_m) {
   HistAcc* h = P.hacc + row;
   for (int i = threadIdx.x; i < 256; i += kThreads) {
@@ -1117,7 +1146,6 @@ __device__ void enter_exact(const Params& P, Smem& sm, int row, const RowP& rp, 
     r.nkeep = 0;
     r.thr_m = thr_m;
   }
-  __threadfence();
   csync();
   publish(P, sm, row);
 }
@@ -1128,40 +1156,6 @@ __device__ __forceinline__ unsigned long long efix(float x, float c1, float c0) 
 }
 
 // ---------------------------------------------------------------- CTA-wide best candidates
-// Merge every compute thread's Top4 into `out` (the same in every thread).
-__device__ void cta_top4(Smem& sm, const Top4& t, Top4& out) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  Cand* wb = reinterpret_cast<Cand*>(sm.u.keys);
-  int head = 0;
-  out.init();
-#pragma unroll
-  for (int round = 0; round < kTC; ++round) {
-    const Cand h = t.at(head);
-    const uint32_t kr = h.r >= 0.f ? __float_as_uint(h.r) + 1u : 0u;
-    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kr);
-    const uint32_t im = __reduce_min_sync(0xFFFFFFFFu, kr == km ? uint32_t(h.id) : 0xFFFFFFFFu);
-    const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kr == km && uint32_t(h.id) == im)) - 1;
-    if (lane == src) wb[warp] = km ? h : Cand{-1.f, 0.f, 1.f, INT_MAX};
-    csync();
-    Cand b{-1.f, 0.f, 1.f, INT_MAX};
-    int bw = -1;
-    for (int w = 0; w < kWarps; ++w) {
-      const Cand c = wb[w];
-      if (c.r >= 0.f && rbetter(c.r, c.id, b.r, b.id)) {
-        b = c;
-        bw = w;
-      }
-    }
-    csync();
-    if (bw < 0) break;
-    out.r[round] = b.r;
-    out.x[round] = b.x;
-    out.E[round] = b.E;
-    out.id[round] = b.id;
-    if (warp == bw && lane == src) ++head;
-  }
-}
-
 __device__ float cta_max_f(Smem& sm, float v) {
   v = warp_max(v);
   if ((threadIdx.x & 31) == 0) sm.red_k[threadIdx.x >> 5] = __float_as_uint(v);
@@ -1207,7 +1201,7 @@ __device__ void cta_part(Smem& sm, double* ms, long long* ct) {
 __device__ __forceinline__ bool row_timed_out(const Params& P, int row) {
   return __ldcg(&P.rowctl[row].timeout) != 0u;
 }
-__device__ void mark_timeout(const Params& P, int row) {
+__device__ __noinline__ void mark_timeout(const Params& P, int row) {
   if (threadIdx.x == 0) {
     atomicOr(&P.rowctl[row].timeout, 1u);
     atomicOr(&P.ctl->err, 1u);
@@ -1224,24 +1218,138 @@ __device__ void load_chunk(const Params& P, Smem& sm, unsigned char* buf, const 
 }
 
 // ---------------------------------------------------------------- finish: chunk records
-template <typename T>
-__device__ void finish_small_k(const Params& P, Smem& sm, int row, const RowP& rp, float c0, float Sf, double S,
-                               float xmax);
+// The row's chunk records (and their mass histograms), staged into the
+// finished chunk's buffer when they fit, else read from L2 on demand.
+struct RecView {
+  const ChunkRec* rec;
+  const float* hist;
+  bool staged;
+  __device__ __forceinline__ ChunkRec get(int c) const {
+    if (staged) return rec[c];
+    union {
+      int4 v[sizeof(ChunkRec) / 16];
+      ChunkRec r;
+    } u;
+    const int4* src = reinterpret_cast<const int4*>(rec + c);
+#pragma unroll
+    for (int i = 0; i < int(sizeof(ChunkRec) / 16); ++i) u.v[i] = __ldcg(src + i);
+    return u.r;
+  }
+  // Mass below bucket threshold B1 of chunk c (histogram bins with Bc - b < B1).
+  __device__ __forceinline__ double mass_below(int c, int Bc, int B1) const {
+    const float4* h = reinterpret_cast<const float4*>(hist + size_t(c) * kBins);
+    double m = 0.0;
+#pragma unroll
+    for (int q = 0; q < kBins / 4; ++q) {
+      const float4 f = staged ? h[q] : __ldcg(h + q);
+      const int b = 4 * q;
+      if (Bc - b < B1) m += double(f.x);
+      if (Bc - b - 1 < B1) m += double(f.y);
+      if (Bc - b - 2 < B1) m += double(f.z);
+      if (Bc - b - 3 < B1) m += double(f.w);
+    }
+    return m;
+  }
+};
+
+__device__ __forceinline__ RecView stage_records(const Params& P, unsigned char* scratch, int row, bool with_hist) {
+  const int NC = P.nc;
+  const size_t rb = size_t(NC) * sizeof(ChunkRec);
+  const size_t hb = with_hist ? size_t(NC) * kBins * sizeof(float) : 0;
+  const ChunkRec* grec = P.rec + size_t(row) * size_t(NC);
+  const float* ghist = P.hist + size_t(row) * size_t(NC) * kBins;
+  RecView v{grec, ghist, false};
+  if (rb + hb <= size_t(kBufBytes)) {
+    int4* d = reinterpret_cast<int4*>(scratch);
+    const int4* src = reinterpret_cast<const int4*>(grec);
+    for (int i = threadIdx.x; i < int(rb / 16); i += kThreads) d[i] = __ldcg(src + i);
+    if (with_hist) {
+      int4* dh = reinterpret_cast<int4*>(scratch + rb);
+      const int4* sh = reinterpret_cast<const int4*>(ghist);
+      for (int i = threadIdx.x; i < int(hb / 16); i += kThreads) dh[i] = __ldcg(sh + i);
+    }
+    v.rec = reinterpret_cast<const ChunkRec*>(scratch);
+    v.hist = reinterpret_cast<const float*>(scratch + rb);
+    v.staged = true;
+  }
+  csync();
+  return v;
+}
+
+// The k-th largest (1-based) high word of keys[0..n), by an 8-bit radix
+// select over shared memory (compute warps).
+__device__ __forceinline__ uint32_t radix_kth(Smem& sm, const unsigned long long* keys, int n, int k) {
+  uint32_t prefix = 0u;
+  int need = k;
+  for (int level = 0; level < 4; ++level) {
+    const int shift = 24 - 8 * level;
+    for (int i = threadIdx.x; i < 256; i += kThreads) sm.u.h.cnt[i] = 0u;
+    csync();
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+      const uint32_t v = uint32_t(keys[i] >> 32);
+      if (level == 0 || (v >> (shift + 8)) == prefix) atomicAdd(&sm.u.h.cnt[(v >> shift) & 255u], 1u);
+    }
+    csync();
+    if (threadIdx.x < 32) {
+      // lane l owns bins 255 - 8l down to 248 - 8l
+      const int lane = threadIdx.x;
+      unsigned c[8];
+      unsigned tot = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = sm.u.h.cnt[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      unsigned incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const unsigned excl = incl - tot;
+      if (excl < unsigned(need) && unsigned(need) <= incl) {
+        unsigned run = excl;
+        int bin = -1;
+        unsigned left = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (bin < 0 && run + c[j] >= unsigned(need)) {
+            bin = 255 - 8 * lane - j;
+            left = unsigned(need) - run;
+          }
+          run += c[j];
+        }
+        sm.bcast_pre = ((long long)bin << 32) | (long long)left;
+      }
+    }
+    csync();
+    const long long bb = sm.bcast_pre;
+    const uint32_t d = uint32_t(bb >> 32);
+    need = int(bb & 0xFFFFFFFFll);
+    prefix = level == 0 ? d : ((prefix << 8) | d);
+    csync();
+  }
+  return prefix;
+}
 
 template <typename T>
-__device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp) {
+__device__ __forceinline__ void finish_small_k(const Params& P, Smem& sm, const RecView& R, unsigned char* scratch, int row,
+                               const RowP& rp, float c0, float Sf, double S, float xmax);
+
+template <typename T>
+__device__ __forceinline__ void finish_stats(const Params& P, Smem& sm, unsigned char* scratch, int row, const RowP& rp) {
   const int tid = threadIdx.x;
   const int NC = P.nc;
   const int64_t V = P.a.vocab;
-  const ChunkRec* recs = P.rec + size_t(row) * size_t(NC);
-  // row max (NaN-aware) and the first chunk holding it
+  const RecView R = stage_records(P, scratch, row, rp.kind == kKindRace && rp.p_on && !rp.k_on && !rp.exact);
+  // row max (NaN-aware), the first chunk with a NaN, the first chunk holding the max
   uint32_t kmax = 0u;
   int nanc = INT_MAX;
   for (int c = tid; c < NC; c += kThreads) {
-    const uint32_t f = __ldcg(&recs[c].flags);
-    if (f & kFEmpty) continue;
-    kmax = max(kmax, nan_key(__ldcg(&recs[c].cmax)));
-    if (f & kFNan) nanc = min(nanc, c);
+    const ChunkRec rc = R.get(c);
+    if (rc.flags & kFEmpty) continue;
+    kmax = max(kmax, nan_key(rc.cmax));
+    if (rc.flags & kFNan) nanc = min(nanc, c);
   }
   kmax = __reduce_max_sync(0xFFFFFFFFu, kmax);
   nanc = __reduce_min_sync(0xFFFFFFFFu, nanc);
@@ -1259,21 +1367,23 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
   csync();
   const bool rnan = nanc != INT_MAX;
   const float xmax = rnan ? __int_as_float(0x7FFFFFFF) : (kmax == 0u ? -INFINITY : key_to_float(kmax));
-  int gc = nanc;
-  if (!rnan) {
-    gc = INT_MAX;
-    for (int c = tid; c < NC; c += kThreads) {
-      if (__ldcg(&recs[c].flags) & kFEmpty) continue;
-      if (__ldcg(&recs[c].cmax) == xmax) gc = min(gc, c);
-    }
-    gc = __reduce_min_sync(0xFFFFFFFFu, gc);
-    if ((tid & 31) == 0) sm.red_i[tid >> 5] = gc;
-    csync();
-    gc = INT_MAX;
-    for (int w = 0; w < kWarps; ++w) gc = min(gc, sm.red_i[w]);
-    csync();
+  const float u = __fmul_rn(xmax, rp.c1);
+  // first chunk holding the max, and the sum S in the row scale
+  int gc = INT_MAX;
+  double part = 0.0;
+  for (int c = tid; c < NC; c += kThreads) {
+    const ChunkRec rc = R.get(c);
+    if (rc.flags & kFEmpty) continue;
+    if (!rnan && rc.cmax == xmax) gc = min(gc, c);
+    if (rc.cmax > -INFINITY && rc.S > 0.0) part += rc.S * exp2_nl(double(rc.u) - double(u));
   }
-  const long long greedy = gc < NC ? (long long)__ldcg(&recs[gc].greedy) : 0;
+  gc = __reduce_min_sync(0xFFFFFFFFu, gc);
+  if ((tid & 31) == 0) sm.red_i[tid >> 5] = gc;
+  const double Ssum = cta_sum_d(sm, part);   // its barriers also publish red_i
+  gc = INT_MAX;
+  for (int w = 0; w < kWarps; ++w) gc = min(gc, sm.red_i[w]);
+  if (rnan) gc = nanc;
+  const long long greedy = gc < NC ? (long long)R.get(gc).greedy : 0;
   if (row_timed_out(P, row)) {
     complete_row(P, row, -1, QE_ROW_TIMEOUT, 0);
     return;
@@ -1282,23 +1392,12 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
     complete_row(P, row, greedy, QE_ROW_GREEDY, 0);
     return;
   }
-  const float u = __fmul_rn(xmax, rp.c1);
   bool finite = !rnan && xmax > -INFINITY && xmax < INFINITY && isfinite(u);
-  double S = 0.0;
-  if (finite) {
-    double part = 0.0;
-    for (int c = tid; c < NC; c += kThreads) {
-      const ChunkRec* r = recs + c;
-      if (__ldcg(&r->flags) & kFEmpty) continue;
-      if (!(__ldcg(&r->cmax) > -INFINITY)) continue;
-      part += __ldcg(&r->S) * exp2(double(__ldcg(&r->u)) - double(u));
-    }
-    S = cta_sum_d(sm, part);
-  }
+  const double S = finite ? Ssum : 0.0;
   const float Sf = float(S);
   if (!(S > 0.0) || !(Sf < INFINITY)) finite = false;
   if (P.a.out_norm && tid == 0)
-    P.a.out_norm[row] = finite ? S * exp2(double(u) - double(xmax) * double(rp.c1))
+    P.a.out_norm[row] = finite ? S * exp2_nl(double(u) - double(xmax) * double(rp.c1))
                                : __longlong_as_double(0x7FF8000000000000LL);
   if (!finite) {
     complete_row(P, row, greedy, QE_ROW_NONFINITE, 0);
@@ -1315,36 +1414,59 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
     return;
   }
   if (rp.kind == kKindSmallK) {
-    finish_small_k<T>(P, sm, row, rp, c0, Sf, S, xmax);
+    finish_small_k<T>(P, sm, R, scratch, row, rp, c0, Sf, S, xmax);
     return;
   }
-  // race rows: exact row-scale ratios of the chunks' candidates
-  Top4 t;
-  t.init();
-  float ceil_row = 0.f;
-  for (int c = tid; c < NC; c += kThreads) {
-    const ChunkRec* r = recs + c;
-    if (__ldcg(&r->flags) & kFEmpty) continue;
-    const int nc = __ldcg(&r->ncand);
-    for (int i = 0; i < nc && i < kR; ++i) {
-      const float x = __ldcg(&r->cand[i].x), E = __ldcg(&r->cand[i].E);
-      const int id = __ldcg(&r->cand[i].id);
-      const float rho = __fdiv_rn(__fdiv_rn(qe_ex2_ftz(__fmaf_rn(x, rp.c1, c0)), Sf), E);
-      t.add(rho, x, E, id);
+  // race rows: warp 0 ranks the chunks' candidates by exact row-scale ratio
+  if ((tid >> 5) == 0) {
+    const int lane = tid & 31;
+    Top4 t;
+    t.init();
+    float cl = 0.f;
+    for (int c = lane; c < NC; c += 32) {
+      const ChunkRec rc = R.get(c);
+      if (rc.flags & kFEmpty) continue;
+      for (int i = 0; i < rc.ncand && i < kR; ++i) {
+        const Cand cd = rc.cand[i];
+        t.add(div_nl(div_nl(qe_ex2_ftz(__fmaf_rn(cd.x, rp.c1, c0)), Sf), cd.E), cd.x, cd.E, cd.id);
+      }
+      if (rc.ceil > 0.f) {
+        // chunk-scale and row-scale exponents differ by the rounding of
+        // x*c1 - u: a few ulps of |u|, plus the ratios' own rounding
+        const double uc = double(rc.u);
+        const double margin = 1.0 + 1.0 / 65536.0 + (fabs(uc) + fabs(double(u))) * (1.0 / 2097152.0);
+        cl = fmaxf(cl, float(double(rc.ceil) * exp2_nl(uc - double(u)) / double(Sf) * margin));
+      }
     }
-    const float cl = __ldcg(&r->ceil);
-    if (cl > 0.f) {
-      // chunk-scale and row-scale exponents differ by the rounding of
-      // x*c1 - u: a few ulps of |u|, plus the ratios' own rounding
-      const double uc = double(__ldcg(&r->u));
-      const double margin = 1.0 + 1.0 / 65536.0 + (fabs(uc) + fabs(double(u))) * (1.0 / 2097152.0);
-      const double cr = double(cl) * exp2(uc - double(u)) / double(Sf) * margin;
-      ceil_row = fmaxf(ceil_row, float(cr));
+    cl = warp_max(cl);
+    int head = 0, n = 0;
+#pragma unroll 1
+    for (int round = 0; round < kTC; ++round) {
+      const Cand h = t.at(head);
+      const uint32_t kr = h.r >= 0.f ? __float_as_uint(h.r) + 1u : 0u;
+      const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kr);
+      if (km == 0u) break;
+      const uint32_t im = __reduce_min_sync(0xFFFFFFFFu, kr == km ? uint32_t(h.id) : 0xFFFFFFFFu);
+      const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kr == km && uint32_t(h.id) == im)) - 1;
+      if (lane == src) {
+        sm.tc[round] = h;
+        ++head;
+      }
+      ++n;
+    }
+    if (lane == 0) {
+      sm.ntc = n;
+      sm.cceil = cl;
     }
   }
-  ceil_row = cta_max_f(sm, ceil_row);
+  csync();
+  const float ceil_row = sm.cceil;
   Top4 top;
-  cta_top4(sm, t, top);
+  top.init();
+  for (int i = 0; i < sm.ntc; ++i) {
+    const Cand c = sm.tc[i];
+    top.add(c.r, c.x, c.E, c.id);
+  }
   int ncomp = 0;
   for (int i = 0; i < kTC; ++i) {
     if (top.r[i] >= 0.f && top.r[i] > ceil_row) ncomp = i + 1;
@@ -1359,10 +1481,21 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
   float xs[kTC];
   int ids[kTC];
   int m = 0;
-  for (int i = 0; i < ncomp; ++i) {
+#pragma unroll
+  for (int i = 0; i < kTC; ++i) {
+    xs[i] = 0.f;
+    ids[i] = INT_MAX;
+  }
+#pragma unroll
+  for (int i = 0; i < kTC; ++i) {
+    if (i >= ncomp) break;
     if (rp.m_on && __fdiv_rn(qe_ex2_ftz(__fmaf_rn(top.x[i], rp.c1, c0)), Sf) < thr_m) continue;
-    xs[m] = top.x[i];
-    ids[m] = top.id[i];
+#pragma unroll
+    for (int j = 0; j < kTC; ++j)
+      if (j == m) {
+        xs[j] = top.x[i];
+        ids[j] = top.id[i];
+      }
     ++m;
   }
   if (m == 0) {
@@ -1380,16 +1513,11 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
     const int B1 = __float2int_rd(fminf(fmaxf(2.f * u1, -1.0e9f), 1.0e9f));
     double L = 0.0;
     for (int c = tid; c < NC; c += kThreads) {
-      const ChunkRec* r = recs + c;
-      if (__ldcg(&r->flags) & kFEmpty) continue;
-      if (!(__ldcg(&r->cmax) > -INFINITY)) continue;
-      const float uc = __ldcg(&r->u);
-      const int Bc = __float2int_rd(fminf(fmaxf(2.f * uc, -1.0e9f), 1.0e9f));
-      const float* hb = P.hist + (size_t(row) * size_t(NC) + size_t(c)) * kBins;
-      double lc = 0.0;
-      for (int b = 0; b < kBins; ++b)
-        if (Bc - b < B1) lc += double(__ldcg(hb + b));
-      L += lc * exp2(double(uc) - double(u)) * (1.0 - 1e-6 - (fabs(double(uc)) + fabs(double(u))) * (1.0 / 2097152.0));
+      const ChunkRec rc = R.get(c);
+      if ((rc.flags & kFEmpty) || !(rc.cmax > -INFINITY)) continue;
+      const int Bc = __float2int_rd(fminf(fmaxf(2.f * rc.u, -1.0e9f), 1.0e9f));
+      L += R.mass_below(c, Bc, B1) * exp2_nl(double(rc.u) - double(u)) *
+           (1.0 - 1e-6 - (fabs(double(rc.u)) + fabs(double(u))) * (1.0 / 2097152.0));
     }
     L = cta_sum_d(sm, L);
     const double ec = double(qe_ex2_ftz(__fmaf_rn(xs[0], rp.c1, c0)));
@@ -1409,8 +1537,8 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
     r.Sf = Sf;
     r.S = S;
     for (int i = 0; i < kTC; ++i) {
-      r.xs[i] = i < m ? xs[i] : 0.f;
-      r.ids[i] = i < m ? ids[i] : INT_MAX;
+      r.xs[i] = xs[i];
+      r.ids[i] = ids[i];
     }
     r.thr_m = thr_m;
   }
@@ -1423,53 +1551,54 @@ __device__ void finish_stats(const Params& P, Smem& sm, int row, const RowP& rp)
 // order (fp64 cumsum rounded to fp32, src/compute/sampler.py:35-37) and
 // min-p element by element, then race over what is kept.
 template <typename T>
-__device__ void finish_small_k(const Params& P, Smem& sm, int row, const RowP& rp, float c0, float Sf, double S,
-                               float xmax) {
+__device__ __forceinline__ void finish_small_k(const Params& P, Smem& sm, const RecView& R, unsigned char* scratch, int row,
+                               const RowP& rp, float c0, float Sf, double S, float xmax) {
   const int tid = threadIdx.x;
   const int NC = P.nc;
   const int64_t V = P.a.vocab;
-  const ChunkRec* recs = P.rec + size_t(row) * size_t(NC);
   const float thr_m = minp_threshold(rp, xmax, c0, Sf);
-  // the largest chunk bound: that chunk alone holds k tokens at or above it
-  uint32_t lkk = 0u;
   int over = 0;
-  for (int c = tid; c < NC; c += kThreads) {
-    const uint32_t f = __ldcg(&recs[c].flags);
-    if (f & kFEmpty) continue;
-    if (f & kFOver) over = 1;
-    lkk = max(lkk, ordered_key(__ldcg(&recs[c].lk)));
-  }
-  lkk = __reduce_max_sync(0xFFFFFFFFu, lkk);
-  over = __reduce_max_sync(0xFFFFFFFFu, over);
-  if ((tid & 31) == 0) {
-    sm.red_k[tid >> 5] = lkk;
-    sm.red_i[tid >> 5] = over;
-  }
+  for (int c = tid; c < NC; c += kThreads)
+    if (R.get(c).flags & kFOver) over = 1;
   if (tid == 0) sm.ngath = 0;
-  csync();
-  lkk = 0u;
-  over = 0;
-  for (int w = 0; w < kWarps; ++w) {
-    lkk = max(lkk, sm.red_k[w]);
-    over |= sm.red_i[w];
-  }
-  csync();
-  if (over) {
+  if (csync_or(over != 0)) {
     enter_exact(P, sm, row, rp, c0, Sf, S, thr_m);
     return;
   }
-  const float Lg = key_to_float(lkk);
+  // the union of the chunks' heads (it holds the row's k largest), in the
+  // chunk buffer after the staged records
+  const size_t roff = R.staged ? (size_t(NC) * sizeof(ChunkRec) + 15) / 16 * 16 : 0;
+  unsigned long long* uk = reinterpret_cast<unsigned long long*>(scratch + roff);
+  const int ucap = int((size_t(kBufBytes) - roff) / sizeof(unsigned long long));
   const GItem* gsrc = P.gather + size_t(row) * size_t(NC) * kGCap;
-  for (int s = tid; s < NC * kGCap; s += kThreads) {
-    const int c = s / kGCap, i = s % kGCap;
-    if (i >= __ldcg(&recs[c].ngather)) continue;
-    const float x = __ldcg(&gsrc[s].x);
-    if (!(x >= Lg)) continue;
-    const int id = __ldcg(&gsrc[s].id);
+  for (int c = 0; c < NC; ++c) {
+    const int ng = R.get(c).ngather;
+    for (int i = tid; i < ng; i += kThreads) {
+      const long long raw = __ldcg(reinterpret_cast<const long long*>(gsrc + size_t(c) * kGCap + i));
+      const float x = __int_as_float(int(raw & 0xFFFFFFFFll));
+      const int id = int(raw >> 32);
+      const int at = atomicAdd(&sm.ngath, 1);
+      if (at < ucap)
+        uk[at] = (static_cast<unsigned long long>(ordered_key(x)) << 32) |
+                 static_cast<unsigned long long>(0xFFFFFFFFu - uint32_t(id));
+    }
+  }
+  csync();
+  const int nu = sm.ngath;
+  if (nu > ucap || nu < int(rp.k)) {
+    csync();
+    enter_exact(P, sm, row, rp, c0, Sf, S, thr_m);
+    return;
+  }
+  // every union key at or above the k-th largest logit
+  const uint32_t tk = radix_kth(sm, uk, nu, int(rp.k));
+  if (tid == 0) sm.ngath = 0;
+  csync();
+  for (int i = tid; i < nu; i += kThreads) {
+    const unsigned long long key = uk[i];
+    if (uint32_t(key >> 32) < tk) continue;
     const int at = atomicAdd(&sm.ngath, 1);
-    if (at < kSortCap)
-      sm.u.keys[at] = (static_cast<unsigned long long>(ordered_key(x)) << 32) |
-                      static_cast<unsigned long long>(0xFFFFFFFFu - uint32_t(id));
+    if (at < kSortCap) sm.u.keys[at] = key;
   }
   csync();
   const int n = sm.ngath;
@@ -1500,15 +1629,12 @@ __device__ void finish_small_k(const Params& P, Smem& sm, int row, const RowP& r
     }
   }
   const int nk = int(rp.k < (long long)n ? rp.k : (long long)n);
-  unsigned long long mykey = tid < nk ? sm.u.keys[tid] : 0ull;
+  const unsigned long long mykey = tid < nk ? sm.u.keys[tid] : 0ull;
   csync();
   const float xi = key_to_float(uint32_t(mykey >> 32));
   const int idi = int(0xFFFFFFFFu - uint32_t(mykey & 0xFFFFFFFFull));
   const float pi = tid < nk ? __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xi, rp.c1, c0)), Sf) : 0.f;
-  if (tid < nk) {
-    sm.u.sk.rho[tid] = pi;
-    sm.u.sk.id[tid] = idi;
-  }
+  if (tid < nk) sm.u.sk.rho[tid] = pi;
   csync();
   if (tid == 0) {
     double cum = 0.0;
@@ -1570,96 +1696,390 @@ __device__ void finish_small_k(const Params& P, Smem& sm, int row, const RowP& r
 }
 
 // ---------------------------------------------------------------- chunk item
+// Warp-level append of finalist codes to the warp's list.
+__device__ __forceinline__ void wappend(uint16_t* fq, int& nf, bool pred, uint32_t code, float hi, float& lc) {
+  const unsigned m = __ballot_sync(0xFFFFFFFFu, pred);
+  if (pred) {
+    const int pos = nf + __popc(m & ((1u << (threadIdx.x & 31)) - 1u));
+    if (pos < kFW) fq[pos] = uint16_t(code);
+    else lc = fmaxf(lc, hi);   // not evaluated: the ceiling keeps the record honest
+  }
+  nf += __popc(m);
+}
+
+// Warp-local race over the warp's two tiles (groups (tile, lane) for
+// tile = warp, warp + kWarps) in the warp's own scale c0s, with the same
+// bounds-first scheme as race_philox: leaves the warp's R best (ratios in
+// that scale) in sm.wl[warp] and a ceiling over its other tokens in
+// sm.wceil[warp].  No CTA barrier.
 template <typename T>
-__device__ void do_chunk(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, bool tmo) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const RowP rp = row_params(P, g.row);
-  uint32_t flags = 0u;
-  float cmax = -INFINITY, u = 0.f, cceil = 0.f, lk = -INFINITY;
-  int greedy = INT_MAX, ncand = 0, ng = 0;
-  double S = 0.0;
-  if (tmo) {
-    mark_timeout(P, g.row);
-    flags = kFEmpty;
-  } else if (g.len <= 0) {
-    flags = kFEmpty;
-  } else {
-    const bool race_row = rp.kind == kKindRace && !rp.exact;
-    const bool smallk = rp.kind == kKindSmallK && !rp.exact;
-    const bool sum = rp.kind != kKindGreedy;
-    if (tid == 0 && race_row && !P.a.noise) set_root(P, sm, g.row);
-    load_chunk<T>(P, sm, buf, g, bulk, rp);
-    G1 sl[2];
-    chunk_pass1<T>(sm, buf, g, rp, sum, sl, &cmax);
-    greedy = chunk_greedy<T>(sm, buf, g, rp, sl, cmax);
-    if (cmax != cmax) flags |= kFNan;
-    if (sum) {
-      u = __fmul_rn(cmax, rp.c1);
-      const bool fin = cmax == cmax && cmax > -INFINITY && cmax < INFINITY && isfinite(u);
-      if (fin) {
-        const bool hist = race_row && rp.p_on;
-        if (hist) {
-          sm.phist[warp][lane] = 0u;
-          sm.phist[warp][lane + 32] = 0u;
-          __syncwarp();
-        }
-        const int Bc = __float2int_rd(fminf(fmaxf(2.f * u, -1.0e9f), 1.0e9f));
-        double part = 0.0;
+__device__ __forceinline__ void race_warp(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g,
+                                          const RowP& rp, float c0s, int R, const G1 sl[2], float e_root,
+                                          long long s_gid, int s_mem) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const NoiseKey key = row_key(P, g.row);
+  const float c1 = rp.c1;
+  if (lane == 0) {
+    for (int i = 0; i < R; ++i) sm.wl[warp][i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
+    sm.wceil[warp] = 0.f;
+  }
+  // A: bounds for the lane's two groups
+  float alo[2], ahi[2], blo[2], bhi[2], ob[2], el2[2];
+  int ag[2], ag2[2], nn[2];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const int tile = warp + kWarps * s;
-          if (tile >= g.ntiles || !(sl[s].gmax > -INFINITY)) continue;
-          const float ug = __fmul_rn(sl[s].gmax, rp.c1);
-          const float term = sl[s].fsum * qe_ex2_ftz(__fsub_rn(ug, u));
-          part += double(term);
-          if (hist) {
-            const int bg = __float2int_rd(fminf(fmaxf(2.f * ug, -1.0e9f), 1.0e9f));
-            const int b = min(kBins - 1, max(0, Bc - bg));
-            atomicAdd(&sm.phist[warp][b], __float2uint_rd(term * 1048576.f));
-          }
-        }
-        S = cta_sum_d(sm, part);
-        if (race_row) {
-          race<T>(P, sm, buf, g, rp, -u, rp.filtered ? kR : 1, Keep{0, 0, 0u, 1, 0});
-          ncand = sm.ncand;
-          cceil = sm.cceil;
-        }
-        if (smallk) {
-          gather_head<T>(sm, buf, g, rp, sl);
-          ng = min(sm.ngath, kGCap);
-          lk = sm.lk;
-          if (sm.over) flags |= kFOver;
-          GItem* dst = P.gather + (size_t(g.row) * size_t(P.nc) + size_t(g.chunk)) * kGCap;
-          for (int i = tid; i < ng; i += kThreads) dst[i] = sm.gl[i];
-        }
-        if (hist && tid < kBins) {
-          unsigned long long q = 0ull;
-          for (int w = 0; w < kWarps; ++w) q += sm.phist[w][tid];
-          P.hist[(size_t(g.row) * size_t(P.nc) + size_t(g.chunk)) * kBins + tid] = __ull2float_rd(q) * 9.5367431640625e-7f;
-        }
+  for (int s = 0; s < 2; ++s) {
+    alo[s] = ahi[s] = blo[s] = bhi[s] = ob[s] = -1.f;
+    el2[s] = 1.f;
+    ag[s] = ag2[s] = nn[s] = 0;
+    const int tile = warp + kWarps * s;
+    if (tile >= g.ntiles) continue;
+    const int lg = tile * 32 + lane;
+    const float gm = sl[s].gmax;
+    const int n = gsize(g.len, tile, lane);
+    nn[s] = n;
+    if (n <= 0 || !(gm > -INFINITY)) continue;
+    const long long gid = g.gbase + lg;
+    const U4 w = philox_at(key, uint32_t(gid), kTagGroup);
+    const bool holds = gid == s_gid;
+    const int a = arg_of(w, n, holds, s_mem);
+    float lo1 = e_root, hi1 = e_root;
+    if (!holds) {
+      const float la = -lg2_approx(uniform_open(w.x)) * 0.6931472f;
+      const float inv = 1.f / float(n);
+      lo1 = (e_root + fmaxf(0.f, la * (1.f - 3e-5f) - 3e-5f) * inv) * (1.f - 2e-6f);
+      hi1 = (e_root + (la * (1.f + 3e-5f) + 3e-5f) * inv) * (1.f + 2e-6f);
+    }
+    ag[s] = a;
+    const float ea = qe_ex2_ftz(__fmaf_rn(xval<T>(sm, buf, rp, tile, lane, a), c1, c0s));
+    alo[s] = __fdividef(ea, hi1) * (1.f - 1e-5f);
+    ahi[s] = __fdividef(ea, lo1) * (1.f + 1e-5f);
+    if (n >= 2) {
+      const float lz = -lg2_approx(uniform_open(w.z)) * 0.6931472f;
+      const float inv1 = 1.f / float(n - 1);
+      const float lo2 = (lo1 + fmaxf(0.f, lz * (1.f - 3e-5f) - 3e-5f) * inv1) * (1.f - 2e-6f);
+      const float hi2 = (hi1 + (lz * (1.f + 3e-5f) + 3e-5f) * inv1) * (1.f + 2e-6f);
+      const int a2 = arg2_of(w, n, a);
+      ag2[s] = a2;
+      el2[s] = lo2;
+      const float eb = qe_ex2_ftz(__fmaf_rn(xval<T>(sm, buf, rp, tile, lane, a2), c1, c0s));
+      blo[s] = __fdividef(eb, hi2) * (1.f - 1e-5f);
+      bhi[s] = __fdividef(eb, lo2) * (1.f + 1e-5f);
+      if (n >= 3) ob[s] = __fdividef(qe_ex2_ftz(__fmaf_rn(gm, c1, c0s)), lo2) * (1.f + 1e-5f);
+    }
+  }
+  // threshold: the warp's R-th largest lower bound
+  float theta = -1.f;
+  {
+    float v0 = alo[0], v1 = blo[0], v2 = alo[1], v3 = blo[1];
+    for (int round = 0; round < R; ++round) {
+      const float m = fmaxf(fmaxf(v0, v1), fmaxf(v2, v3));
+      const float wm = warp_max(m);
+      theta = wm;
+      const unsigned bal = __ballot_sync(0xFFFFFFFFu, m == wm);
+      if (lane == __ffs(bal) - 1) {
+        if (v0 == wm) v0 = -1.f;
+        else if (v1 == wm) v1 = -1.f;
+        else if (v2 == wm) v2 = -1.f;
+        else v3 = -1.f;
       }
     }
   }
-  if (tid == 0) {
+  // B: finalists and expansions
+  uint16_t* fq = sm.fqw[warp];
+  int nf = 0;
+  float lc = 0.f;
+  bool ex[2];
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const uint32_t lg = uint32_t((warp + kWarps * s) * 32 + lane);
+    const bool pa = ahi[s] >= 0.f && ahi[s] >= theta, pb = bhi[s] >= 0.f && bhi[s] >= theta;
+    if (ahi[s] >= 0.f && !pa) lc = fmaxf(lc, ahi[s]);
+    if (bhi[s] >= 0.f && !pb) lc = fmaxf(lc, bhi[s]);
+    wappend(fq, nf, pa, uint32_t(kFinA << 14) | (lg << 5), ahi[s], lc);
+    wappend(fq, nf, pb, uint32_t(kFinB << 14) | (lg << 5), bhi[s], lc);
+    ex[s] = ob[s] >= 0.f && ob[s] >= theta;
+    if (ob[s] >= 0.f && !ex[s]) lc = fmaxf(lc, ob[s]);
+  }
+  // C: expansions, one group at a time, lanes over its members
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    unsigned em = __ballot_sync(0xFFFFFFFFu, ex[s]);
+    while (em) {
+      const int src = __ffs(em) - 1;
+      em &= em - 1u;
+      const int tile = warp + kWarps * s;
+      const int n = __shfl_sync(0xFFFFFFFFu, nn[s], src);
+      const int a = __shfl_sync(0xFFFFFFFFu, ag[s], src), a2 = __shfl_sync(0xFFFFFFFFu, ag2[s], src);
+      const float e2lo = __shfl_sync(0xFFFFFFFFu, el2[s], src);
+      const int m = lane;
+      bool pm = false;
+      float bm = 0.f;
+      if (m < n && m != a && m != a2) {
+        bm = __fdividef(qe_ex2_ftz(__fmaf_rn(xval<T>(sm, buf, rp, tile, src, m), c1, c0s)), e2lo) * (1.f + 1e-5f);
+        pm = bm >= theta;
+        if (!pm) lc = fmaxf(lc, bm);
+      }
+      wappend(fq, nf, pm, uint32_t(kFinT << 14) | uint32_t((tile * 32 + src) << 5) | uint32_t(m), bm, lc);
+    }
+  }
+  __syncwarp();
+  // D: exact noise for the finalists
+  const int nfc = min(nf, kFW);
+  for (int base = 0; base < nfc; base += 32) {
+    const int e = base + lane;
+    Cand c{-1.f, 0.f, 1.f, INT_MAX};
+    if (e < nfc) c = finalist<T>(sm, buf, g, rp, key, c0s, fq[e]);
+    warp_offer(sm.wl[warp], &sm.wceil[warp], R, c.r, c.x, c.E, c.id);
+  }
+  raise_ceiling(sm, lc);
+}
+
+// Caller-noise version (parity mode): dense over the warp's tokens.
+template <typename T>
+__device__ __forceinline__ void race_noise_warp(const Params& P, Smem& sm, const unsigned char* buf, const Geo& g,
+                                                const RowP& rp, float c0s, int R, const G1 sl[2]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float c1 = rp.c1;
+  if (lane == 0) {
+    for (int i = 0; i < R; ++i) sm.wl[warp][i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
+    sm.wceil[warp] = 0.f;
+  }
+  Top4 best;
+  best.init();
+  float lc = 0.f;
+  const float* nz = P.a.noise + size_t(g.row) * size_t(P.a.noise_ld) + size_t(g.start);
+#pragma unroll 1
+  for (int s = 0; s < 2; ++s) {
+    const int tile = warp + kWarps * s;
+    if (tile >= g.ntiles || !(sl[s].gmax > -INFINITY)) continue;
+    const int n = gsize(g.len, tile, lane);
+#pragma unroll 1
+    for (int m = 0; m < n; ++m) {
+      const int o = moff(tile, lane, m);
+      const float x = xval<T>(sm, buf, rp, tile, lane, m);
+      const float ev = qe_ex2_ftz(__fmaf_rn(x, c1, c0s));
+      const float E = __ldg(nz + o);
+      const float ap = __fdividef(ev, E) * (1.f + 1e-5f);
+      if (!(ap >= best.r[kTC - 1])) {
+        lc = fmaxf(lc, ap);
+        continue;
+      }
+      const float r = div_nl(ev, E);
+      if (best.r[kTC - 1] >= 0.f && !rbetter(r, int(g.start + o), best.r[kTC - 1], best.id[kTC - 1])) {
+        lc = fmaxf(lc, r);
+        continue;
+      }
+      if (best.r[kTC - 1] >= 0.f) lc = fmaxf(lc, best.r[kTC - 1]);
+      best.add(r, x, E, int(g.start + o));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kTC; ++i) warp_offer(sm.wl[warp], &sm.wceil[warp], R, best.r[i], best.x[i], best.E[i], best.id[i]);
+  raise_ceiling(sm, lc);
+}
+
+template <typename T>
+__device__ __forceinline__ void do_chunk(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk,
+                                         const RowP& rp, bool tmo, float e_root, long long s_gid, int s_mem) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  ChunkRec* rec = P.rec + size_t(g.row) * size_t(P.nc) + size_t(g.chunk);
+  if (tmo || g.len <= 0) {
+    if (tmo) mark_timeout(P, g.row);
+    if (tid == 0) {
+      ChunkRec r;
+      r.cmax = -INFINITY;
+      r.u = 0.f;
+      r.greedy = INT_MAX;
+      r.flags = kFEmpty;
+      r.S = 0.0;
+      r.ceil = 0.f;
+      r.ncand = 0;
+      r.lk = -INFINITY;
+      r.ngather = 0;
+      for (int i = 0; i < kR; ++i) r.cand[i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
+      *rec = r;
+    }
+    return;
+  }
+  const bool race_row = rp.kind == kKindRace && !rp.exact;
+  const bool smallk = rp.kind == kKindSmallK && !rp.exact;
+  const bool sum = rp.kind != kKindGreedy;
+  const int R = rp.filtered ? kR : 1;
+  // tail beyond the bulk copy, padding, repetition-penalty bits
+  const bool pad = bulk < g.ntiles * kTile;
+  if (pad) fill_chunk<T>(P, buf, g, bulk);
+  if (rp.pen) build_pen(sm, g, rp);
+  else if (pad) csync();
+  // pass 1 and the race, warp by warp in each warp's own scale
+  G1 sl[2];
+  uint32_t wkey = 0u;
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    sl[s] = G1{-INFINITY, 0.f};
+    const int tile = warp + kWarps * s;
+    if (tile < g.ntiles) {
+      sl[s] = pass1<T>(sm, buf, rp, tile, lane, sum);
+      wkey = max(wkey, nan_key(sl[s].gmax));
+    }
+  }
+  wkey = __reduce_max_sync(0xFFFFFFFFu, wkey);
+  const float wmax = wkey == 0xFFFFFFFFu ? __int_as_float(0x7FFFFFFF) : (wkey == 0u ? -INFINITY : key_to_float(wkey));
+  const float uw = sum ? __fmul_rn(wmax, rp.c1) : 0.f;
+  const bool wfin = sum && wmax == wmax && wmax > -INFINITY && wmax < INFINITY && isfinite(uw);
+  const bool hist = race_row && rp.p_on && !rp.k_on;
+  double sw = 0.0;
+  if (wfin) {
+    if (hist) {
+      sm.phist[warp][lane] = 0u;
+      sm.phist[warp][lane + 32] = 0u;
+      __syncwarp();
+    }
+    const int Bw = __float2int_rd(fminf(fmaxf(2.f * uw, -1.0e9f), 1.0e9f));
+    float part = 0.f;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (warp + kWarps * s >= g.ntiles || !(sl[s].gmax > -INFINITY)) continue;
+      const float ug = __fmul_rn(sl[s].gmax, rp.c1);
+      const float term = sl[s].fsum * qe_ex2_ftz(__fsub_rn(ug, uw));
+      part += term;
+      if (hist) {
+        const int bg = __float2int_rd(fminf(fmaxf(2.f * ug, -1.0e9f), 1.0e9f));
+        atomicAdd(&sm.phist[warp][min(kBins - 1, max(0, Bw - bg))], __float2uint_rd(term * 1048576.f));
+      }
+    }
+    sw = double(part);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sw += __shfl_xor_sync(0xFFFFFFFFu, sw, o);
+    if (race_row) {
+      if (P.a.noise) race_noise_warp<T>(P, sm, buf, g, rp, -uw, R, sl);
+      else race_warp<T>(P, sm, buf, g, rp, -uw, R, sl, e_root, s_gid, s_mem);
+    }
+  } else if (race_row && lane == 0) {
+    for (int i = 0; i < R; ++i) sm.wl[warp][i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
+    sm.wceil[warp] = 0.f;
+  }
+  if (lane == 0) {
+    sm.wr_key[warp] = wkey;
+    sm.wr_u[warp] = uw;
+    sm.wr_S[warp] = wfin ? sw : 0.0;
+  }
+  csync();
+  // chunk max, its anchor, and what needs the whole CTA
+  uint32_t ckey = 0u;
+  for (int w = 0; w < kWarps; ++w) ckey = max(ckey, sm.wr_key[w]);
+  const float cmax = ckey == 0xFFFFFFFFu ? __int_as_float(0x7FFFFFFF) : (ckey == 0u ? -INFINITY : key_to_float(ckey));
+  const float u = sum ? __fmul_rn(cmax, rp.c1) : 0.f;
+  const bool fin = sum && cmax == cmax && cmax > -INFINITY && cmax < INFINITY && isfinite(u);
+  int greedy = INT_MAX;
+  // the first id of the chunk max matters only to greedy rows and to rows
+  // that turn out not finite (a non-finite row's max chunk is not finite)
+  if (!fin || rp.kind == kKindArgmax) greedy = chunk_greedy<T>(sm, buf, g, rp, sl, cmax);
+  int ng = 0;
+  float lk = -INFINITY;
+  uint32_t flags = cmax != cmax ? kFNan : 0u;
+  if (smallk && fin) {
+    gather_head<T>(sm, buf, g, rp, sl);
+    ng = min(sm.ngath, kGCap);
+    lk = sm.lk;
+    if (sm.over) flags |= kFOver;
+    GItem* dst = P.gather + (size_t(g.row) * size_t(P.nc) + size_t(g.chunk)) * kGCap;
+    for (int i = tid; i < ng; i += kThreads) dst[i] = sm.gl[i];
+  }
+  if (warp != 0) return;
+  // warp 0: merge the warps into the chunk record (rescaled to the chunk's anchor)
+  double S = 0.0;
+  float cl = 0.f;
+  int ncand = 0;
+  Cand out[kR];
+#pragma unroll
+  for (int i = 0; i < kR; ++i) out[i] = Cand{-1.f, 0.f, 1.f, INT_MAX};
+  if (fin) {
+    if (lane < kWarps) {
+      const float ul = sm.wr_u[lane];
+      const double sl_ = sm.wr_S[lane];
+      const double sc = sl_ > 0.0 ? sl_ * double(qe_ex2_ftz(__fsub_rn(ul, u))) : 0.0;
+      S = sc;
+      if (race_row) {
+        const float wc = sm.wceil[lane];
+        if (wc > 0.f) {
+          const double margin = 1.0 + 1.0 / 65536.0 + (fabs(double(ul)) + fabs(double(u))) * (1.0 / 2097152.0);
+          cl = float(double(wc) * double(qe_ex2_ftz(__fsub_rn(ul, u))) * margin);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xFFFFFFFFu, S, o);
+    if (race_row) {
+      // each warp's candidates, re-ranked by their exact chunk-scale ratio
+      Cand c{-1.f, 0.f, 1.f, INT_MAX};
+      if (lane < kWarps * R) {
+        const Cand w = sm.wl[lane / R][lane % R];
+        if (w.r >= 0.f) c = Cand{div_nl(qe_ex2_ftz(__fmaf_rn(w.x, rp.c1, -u)), w.E), w.x, w.E, w.id};
+      }
+      uint32_t kr = c.r >= 0.f ? __float_as_uint(c.r) + 1u : 0u;
+#pragma unroll
+      for (int i = 0; i < kR; ++i) {
+        if (i >= R) break;
+        const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kr);
+        if (km == 0u) break;
+        const uint32_t im = __reduce_min_sync(0xFFFFFFFFu, kr == km ? uint32_t(c.id) : 0xFFFFFFFFu);
+        const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kr == km && uint32_t(c.id) == im)) - 1;
+        out[i] = Cand{__shfl_sync(0xFFFFFFFFu, c.r, src), __shfl_sync(0xFFFFFFFFu, c.x, src),
+                      __shfl_sync(0xFFFFFFFFu, c.E, src), int(im)};
+        if (lane == src) kr = 0u;
+        ++ncand;
+      }
+      if (kr) cl = fmaxf(cl, c.r);
+      cl = warp_max(cl);
+    }
+    if (hist) {
+      // chunk bins from the warps' bins: shift each by its anchor difference
+      // and rescale its mass to the chunk's anchor, rounding down (the bins
+      // are lower bounds)
+      const int Bc = __float2int_rd(fminf(fmaxf(2.f * u, -1.0e9f), 1.0e9f));
+      float* hb = P.hist + (size_t(g.row) * size_t(P.nc) + size_t(g.chunk)) * kBins;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = lane + 32 * h;
+        double q = 0.0;
+        for (int w = 0; w < kWarps; ++w) {
+          if (sm.wr_S[w] <= 0.0) continue;
+          const float uwl = sm.wr_u[w];
+          const int sh = Bc - __float2int_rd(fminf(fmaxf(2.f * uwl, -1.0e9f), 1.0e9f));
+          unsigned long long qw = 0ull;
+          if (j < kBins - 1) {
+            const int b = j - sh;
+            if (b >= 0) qw = sm.phist[w][b];
+          } else {
+            for (int b = max(0, kBins - 1 - sh); b < kBins; ++b) qw += sm.phist[w][b];
+          }
+          if (qw)
+            q += double(qw) * double(qe_ex2_ftz(__fsub_rn(uwl, u))) *
+                 (1.0 - 1.0 / 65536.0 - (fabs(double(uwl)) + fabs(double(u))) * (1.0 / 2097152.0));
+        }
+        hb[j] = __double2float_rd(q * (1.0 / 1048576.0));
+      }
+    }
+  }
+  if (lane == 0) {
     ChunkRec r;
     r.cmax = cmax;
     r.u = u;
     r.greedy = greedy;
     r.flags = flags;
     r.S = S;
-    r.ceil = cceil;
+    r.ceil = cl;
     r.ncand = ncand;
     r.lk = lk;
     r.ngather = ng;
-    for (int i = 0; i < kR; ++i) r.cand[i] = i < ncand ? sm.cand[i] : Cand{-1.f, 0.f, 1.f, INT_MAX};
-    P.rec[size_t(g.row) * size_t(P.nc) + size_t(g.chunk)] = r;
+    for (int i = 0; i < kR; ++i) r.cand[i] = out[i];
+    *rec = r;
   }
-  if (arrive(P, sm, g.row)) finish_stats<T>(P, sm, g.row, rp);
 }
 
 // ---------------------------------------------------------------- test round
 template <typename T>
-__device__ void finish_test(const Params& P, Smem& sm, int row, const RowP& rp) {
+__device__ __forceinline__ void finish_test(const Params& P, Smem& sm, int row, const RowP& rp) {
   const int NC = P.nc;
   double ms[kTC] = {0.0, 0.0, 0.0, 0.0};
   long long ct[kTC] = {0, 0, 0, 0};
@@ -1690,7 +2110,7 @@ __device__ void finish_test(const Params& P, Smem& sm, int row, const RowP& rp) 
 }
 
 template <typename T>
-__device__ void do_test(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
+__device__ __forceinline__ void do_test(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
                         bool tmo) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const RowRound& rr = sm.rr;
@@ -1741,12 +2161,11 @@ __device__ void do_test(const Params& P, Smem& sm, unsigned char* buf, const Geo
       q->cnt[i] = ct[i];
     }
   }
-  if (arrive(P, sm, g.row)) finish_test<T>(P, sm, g.row, rp);
 }
 
 // ---------------------------------------------------------------- exact rounds: radix histogram
 template <typename T>
-__device__ void finish_hist(const Params& P, Smem& sm, int row, const RowP& rp) {
+__device__ __forceinline__ void finish_hist(const Params& P, Smem& sm, int row, const RowP& rp) {
   const int tid = threadIdx.x;
   HistAcc* h = P.hacc + row;
   for (int i = tid; i < 256; i += kThreads) {
@@ -1831,14 +2250,13 @@ __device__ void finish_hist(const Params& P, Smem& sm, int row, const RowP& rp) 
       h->mass[i] = 0ull;
     }
     if (tid == 0) h->nm = 0u;
-    __threadfence();
   }
   csync();
   publish(P, sm, row);
 }
 
 template <typename T>
-__device__ void do_hist(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
+__device__ __forceinline__ void do_hist(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
                         bool tmo) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowRound& rr = sm.rr;
@@ -1888,38 +2306,45 @@ __device__ void do_hist(const Params& P, Smem& sm, unsigned char* buf, const Geo
     }
   }
   if (tid == 0 && sm.u.h.nm) atomicAdd(&h->nm, sm.u.h.nm);
-  if (arrive(P, sm, g.row)) finish_hist<T>(P, sm, g.row, rp);
 }
 
 // ---------------------------------------------------------------- exact rounds: ties at the boundary
 template <typename T>
-__device__ void finish_ties(const Params& P, Smem& sm, int row, const RowP& rp) {
+__device__ __forceinline__ void finish_ties(const Params& P, Smem& sm, int row, const RowP& rp) {
   const int NC = P.nc;
   if (row_timed_out(P, row)) {
     complete_row(P, row, -1, QE_ROW_TIMEOUT, 0);
     return;
   }
-  if (threadIdx.x == 0) {
-    long long pre = 0;
-    const long long kt = sm.rr.kties;
-    for (int c = 0; c < NC; ++c) {
-      Part* q = P.part + size_t(row) * size_t(NC) + size_t(c);
-      const long long n = __ldcg(&q->cnt[0]);
-      long long allow = kt - pre;
-      allow = allow < 0 ? 0 : (allow > n ? n : allow);
-      q->cnt[1] = allow;
-      q->cnt[2] = n;
-      pre += n;
+  // chunk tie counts in id order -> how many of its ties each chunk keeps
+  long long* cnt = reinterpret_cast<long long*>(sm.u.keys);
+  for (int c0 = 0; c0 < NC; c0 += kSortCap) {
+    for (int c = c0 + threadIdx.x; c < NC && c < c0 + kSortCap; c += kThreads)
+      cnt[c - c0] = __ldcg(&P.part[size_t(row) * size_t(NC) + size_t(c)].cnt[0]);
+    csync();
+    if (threadIdx.x == 0) {
+      long long pre = c0 == 0 ? 0 : sm.bcast_pre;
+      const long long kt = sm.rr.kties;
+      for (int c = c0; c < NC && c < c0 + kSortCap; ++c) {
+        Part* q = P.part + size_t(row) * size_t(NC) + size_t(c);
+        const long long n = cnt[c - c0];
+        long long allow = kt - pre;
+        allow = allow < 0 ? 0 : (allow > n ? n : allow);
+        q->cnt[1] = allow;
+        q->cnt[2] = n;
+        pre += n;
+      }
+      sm.bcast_pre = pre;
     }
-    sm.rr.type = kRoundRace;
-    __threadfence();
+    csync();
   }
+  if (threadIdx.x == 0) sm.rr.type = kRoundRace;
   csync();
   publish(P, sm, row);
 }
 
 template <typename T>
-__device__ void do_ties(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
+__device__ __forceinline__ void do_ties(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
                         bool tmo) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const RowRound& rr = sm.rr;
@@ -1942,13 +2367,12 @@ __device__ void do_ties(const Params& P, Smem& sm, unsigned char* buf, const Geo
   }
   cnt = cta_sum_l(sm, cnt);
   if (threadIdx.x == 0) P.part[size_t(g.row) * size_t(P.nc) + size_t(g.chunk)].cnt[0] = cnt;
-  if (arrive(P, sm, g.row)) finish_ties<T>(P, sm, g.row, rp);
 }
 
 // Tie ranks of the chunk: bit o of bits[] marks offset o as a boundary tie;
 // pre[w] counts the ties in words before w.
 template <typename T>
-__device__ void build_ties(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, int sh, uint32_t kkey,
+__device__ __forceinline__ void build_ties(Smem& sm, const unsigned char* buf, const Geo& g, const RowP& rp, int sh, uint32_t kkey,
                            const G1 sl[2]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = g.ntiles * 32;
@@ -1994,7 +2418,7 @@ __device__ void build_ties(Smem& sm, const unsigned char* buf, const Geo& g, con
 
 // ---------------------------------------------------------------- exact rounds: race over the kept set
 template <typename T>
-__device__ void finish_race(const Params& P, Smem& sm, int row, const RowP& rp) {
+__device__ __forceinline__ void finish_race(const Params& P, Smem& sm, int row, const RowP& rp) {
   const int tid = threadIdx.x, NC = P.nc;
   float br = -1.f;
   int bid = INT_MAX;
@@ -2035,7 +2459,7 @@ __device__ void finish_race(const Params& P, Smem& sm, int row, const RowP& rp) 
 }
 
 template <typename T>
-__device__ void do_race_round(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
+__device__ __forceinline__ void do_race_round(const Params& P, Smem& sm, unsigned char* buf, const Geo& g, int bulk, const RowP& rp,
                               bool tmo) {
   const RowRound& rr = sm.rr;
   float rho = -1.f;
@@ -2043,7 +2467,6 @@ __device__ void do_race_round(const Params& P, Smem& sm, unsigned char* buf, con
   if (tmo) {
     mark_timeout(P, g.row);
   } else if (g.len > 0) {
-    if (threadIdx.x == 0 && !P.a.noise) set_root(P, sm, g.row);
     load_chunk<T>(P, sm, buf, g, bulk, rp);
     Keep kp{1, 24 - 8 * rr.level, rr.kkey, rr.ties_all, 0};
     bool need_bits = false;
@@ -2073,124 +2496,235 @@ __device__ void do_race_round(const Params& P, Smem& sm, unsigned char* buf, con
     q->mass[0] = double(rho);
     q->cnt[0] = rid;
   }
-  if (arrive(P, sm, g.row)) finish_race<T>(P, sm, g.row, rp);
 }
 
 // ---------------------------------------------------------------- work loop
-template <typename T>
-__device__ void process(const Params& P, Smem& sm, int b, long long item, bool tmo) {
-  unsigned char* buf = sm.buf[b];
-  const int bulk = sm.bulk_elems[b];
-  if (item >= 0) {
-    do_chunk<T>(P, sm, buf, geo_of(P, int(item / P.nc), int(item % P.nc)), bulk, tmo);
-    return;
-  }
-  const long long j = -2 - item;
-  const int row = sm.frow[b];
-  const Geo g = geo_of(P, row, int(j % P.nc));
+__device__ __forceinline__ void copy_round(const Params& P, Smem& sm, int row) {
   static_assert(sizeof(RowRound) % 16 == 0 && sizeof(RowRound) / 16 <= kThreads, "RowRound copy");
   if (threadIdx.x < sizeof(RowRound) / 16)
     reinterpret_cast<int4*>(&sm.rr)[threadIdx.x] = __ldcg(reinterpret_cast<const int4*>(P.round + row) + threadIdx.x);
   csync();
-  const RowP rp = row_params(P, row);
-  switch (sm.rr.type) {
-    case kRoundTest: do_test<T>(P, sm, buf, g, bulk, rp, tmo); break;
-    case kRoundHist: do_hist<T>(P, sm, buf, g, bulk, rp, tmo); break;
-    case kRoundTies: do_ties<T>(P, sm, buf, g, bulk, rp, tmo); break;
-    default: do_race_round<T>(P, sm, buf, g, bulk, rp, tmo); break;
-  }
 }
 
-// Claim the next item: follow-up items first (they re-read chunks that are
-// still in L2), then chunk items.  Returns -1 once every row is done.
-__device__ void claim(const Params& P, long long& item, int& frow) {
+// One item on the compute warps.  Returns the row whose part was filed (the
+// producer turns it into an arrival), or -1.
+template <typename T>
+__device__ int process(const Params& P, Smem& sm, int b, int kind, bool tmo) {
+  unsigned char* buf = sm.buf[b];
+  const int bulk = sm.bulk_elems[b];
+  const RowP& rp = sm.rowp[b];
+  const int row = sm.frow[b];
+  if (threadIdx.x == 0) {
+    sm.e_root = sm.root_e[b];
+    sm.s_gid = sm.root_gid[b];
+    sm.s_mem = sm.root_mem[b];
+  }
+  if (kind == kItemChunk) {
+    do_chunk<T>(P, sm, buf, geo_of(P, row, sm.chunk[b]), bulk, rp, tmo, sm.root_e[b], sm.root_gid[b],
+                sm.root_mem[b]);
+    return row;
+  }
+  if (kind == kItemFollow) {
+    const Geo g = geo_of(P, row, sm.chunk[b]);
+    copy_round(P, sm, row);
+    switch (sm.rr.type) {
+      case kRoundTest: do_test<T>(P, sm, buf, g, bulk, rp, tmo); break;
+      case kRoundHist: do_hist<T>(P, sm, buf, g, bulk, rp, tmo); break;
+      case kRoundTies: do_ties<T>(P, sm, buf, g, bulk, rp, tmo); break;
+      default: do_race_round<T>(P, sm, buf, g, bulk, rp, tmo); break;
+    }
+    return row;
+  }
+  // finish the row's current round (this CTA's producer saw its last part)
+  csync();
+  const unsigned rt = __ldcg(&P.rowctl[row].round);
+  if (rt == 0u) {
+    finish_stats<T>(P, sm, buf, row, rp);
+    return -1;
+  }
+  copy_round(P, sm, row);
+  switch (sm.rr.type) {
+    case kRoundTest: finish_test<T>(P, sm, row, rp); break;
+    case kRoundHist: finish_hist<T>(P, sm, row, rp); break;
+    case kRoundTies: finish_ties<T>(P, sm, row, rp); break;
+    default: finish_race<T>(P, sm, row, rp); break;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ unsigned int atom_add_release(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0u;
+}
+
+// Claim work: follow-up items first (they re-read chunks still in L2), then
+// this CTA's next chunk item (CTA c takes chunk items c, c + grid, ...).
+// Sets kind = kItemNone when there is nothing to hand out right now.
+__device__ void claim(const Params& P, unsigned int& next_chunk, int& kind, int& chunk, int& row) {
   const unsigned nc = unsigned(P.nc);
   const unsigned B = unsigned(P.a.batch);
-  uint32_t spins = 0;
-  while (true) {
-    const unsigned qe = min(ld_acquire(&P.ctl->qentries), B * unsigned(kMaxRounds));
-    const unsigned long long avail = (unsigned long long)qe * nc;
-    unsigned qh = ld_relaxed(&P.ctl->qhead);
-    while ((unsigned long long)qh < avail) {
-      const unsigned prev = atomicCAS(&P.ctl->qhead, qh, qh + 1u);
-      if (prev == qh) {
-        const unsigned e = qh / nc;
-        unsigned v = 0u;
-        for (uint32_t w = 0; w < P.polls; ++w) {
-          v = ld_acquire(&P.queue[e]);
-          if (v) break;
-          __nanosleep(64);
-        }
-        if (!v) {
-          atomicOr(&P.ctl->err, 1u);
-          item = -1;
-          return;
-        }
-        item = -2 - (long long)qh;
-        frow = int(v - 1u);
+  kind = kItemNone;
+  const unsigned qe = min(ld_relaxed(&P.ctl->qentries), B * unsigned(kMaxRounds));
+  const unsigned long long avail = (unsigned long long)qe * nc;
+  unsigned qh = ld_relaxed(&P.ctl->qhead);
+  while ((unsigned long long)qh < avail) {
+    const unsigned prev = atomicCAS(&P.ctl->qhead, qh, qh + 1u);
+    if (prev == qh) {
+      const unsigned e = qh / nc;
+      unsigned v = 0u;
+      for (uint32_t w = 0; w < P.polls; ++w) {
+        v = ld_acquire(&P.queue[e]);
+        if (v) break;
+        __nanosleep(64);
+      }
+      if (!v) {
+        atomicOr(&P.ctl->err, 1u);
+        kind = kItemEnd;
         return;
       }
-      qh = prev;
-    }
-    if (ld_relaxed(&P.ctl->next) < P.nitems) {
-      const unsigned s = atomicAdd(&P.ctl->next, 1u);
-      if (s < P.nitems) {
-        item = s;
-        return;
-      }
-    }
-    if (ld_acquire(&P.ctl->rows_done) >= B) {
-      item = -1;
+      kind = kItemFollow;
+      row = int(v - 1u);
+      chunk = int(qh % nc);
       return;
     }
-    if (++spins > P.polls) {
-      atomicOr(&P.ctl->err, 1u);
-      item = -1;
-      return;
-    }
-    __nanosleep(200);
+    qh = prev;
+  }
+  if (next_chunk < P.nitems) {
+    kind = kItemChunk;
+    row = int(next_chunk / nc);
+    chunk = int(next_chunk % nc);
+    next_chunk += gridDim.x;
   }
 }
 
-// The producer warp: claims items and moves their chunks into the buffers.
+// File one arrival for `row` (release) and report whether it was the last.
+__device__ __forceinline__ unsigned int file_arrival(const Params& P, int row) {
+  return atom_add_release(&P.rowctl[row].cnt, 1u);
+}
+
+// The producer warp (lane 0): decides each buffer's next item, prefetches
+// the row's parameters and noise root, moves chunks in with bulk copies, and
+// files the compute warps' parts as arrivals, so the compute warps never wait
+// on a global round trip.  An arrival whose result shows the row's last part
+// becomes a finish item for this CTA.
 __device__ void producer(const Params& P, Smem& sm) {
   if ((threadIdx.x & 31) != 0) return;
+  const unsigned nc = unsigned(P.nc);
   uint32_t eph[kNumBuf] = {0u, 0u};
-  bool used[kNumBuf] = {false, false};
+  bool busy[kNumBuf] = {false, false};   // handed to the compute warps, not yet released
   int b = 0;
+  unsigned int next_chunk = blockIdx.x;
+  int fq_head = 0, fq_tail = 0;
+  int pend_row = -1;
+  unsigned int pend_old = 0u;
+  uint32_t idle = 0;
   while (true) {
-    if (used[b]) {
+    // the arrival filed last round: was it the row's last part?
+    if (pend_row >= 0) {
+      if (pend_old == nc - 1u) {
+        fence_acq_rel();
+        sm.finq[fq_tail++ % kFinQ] = pend_row;
+      }
+      pend_row = -1;
+    }
+    int kind = kItemNone, chunk = 0, row = -1;
+    if (fq_head != fq_tail) {
+      kind = kItemFinish;
+      row = sm.finq[fq_head++ % kFinQ];
+    } else {
+      claim(P, next_chunk, kind, chunk, row);
+    }
+    if (kind == kItemNone) {
+      // nothing to hand out: file the parts of released buffers, then retry or end
+      bool progress = false;
+      for (int x = 0; x < kNumBuf; ++x) {
+        if (busy[x] && mbar_test(&sm.empty[x], eph[x])) {
+          eph[x] ^= 1u;
+          busy[x] = false;
+          const int r = sm.mail[x];
+          if (r >= 0 && file_arrival(P, r) == nc - 1u) {
+            fence_acq_rel();
+            sm.finq[fq_tail++ % kFinQ] = r;
+          }
+          progress = true;
+        }
+      }
+      if (progress || fq_head != fq_tail) continue;
+      if (ld_acquire(&P.ctl->rows_done) >= unsigned(P.a.batch)) {
+        kind = kItemEnd;
+      } else if (++idle > P.polls) {
+        atomicOr(&P.ctl->err, 1u);
+        kind = kItemEnd;
+      } else {
+        __nanosleep(256);
+        continue;
+      }
+    }
+    idle = 0;
+    // what the compute warps need, fetched before the buffer is free
+    RowP rp;
+    float re = 0.f;
+    long long rg = -1;
+    int rm = 0;
+    if (kind != kItemEnd) {
+      rp = row_params(P, row);
+      if (!P.a.noise && kind != kItemFinish) {
+        const NoiseKey key = row_key(P, row);
+        const NoiseRoot rt = noise_root(key, P.a.vocab);
+        re = rt.e_root;
+        int64_t gs = -1;
+        token_group_p(P, rt.s, &gs, &rm);
+        rg = gs;
+      }
+    }
+    if (busy[b]) {
       if (!mbar_wait(&sm.empty[b], eph[b], P.polls)) {
         atomicOr(&P.ctl->err, 1u);
         return;
       }
       eph[b] ^= 1u;
+      busy[b] = false;
+      const int r = sm.mail[b];
+      if (r >= 0) {
+        pend_old = file_arrival(P, r);   // checked next round
+        pend_row = r;
+      }
     }
-    long long item = -1;
-    int frow = -1;
-    claim(P, item, frow);
-    sm.item[b] = item;
-    sm.frow[b] = frow;
-    if (item == -1) {
-      mbar_arrive(&sm.full[b]);
-      return;
-    }
-    const int row = item >= 0 ? int(item / P.nc) : frow;
-    const int chunk = item >= 0 ? int(item % P.nc) : int((-2 - item) % P.nc);
-    const Geo g = geo_of(P, row, chunk);
+    sm.kind[b] = kind;
+    sm.chunk[b] = chunk;
+    sm.frow[b] = row;
+    sm.rowp[b] = rp;
+    sm.root_e[b] = re;
+    sm.root_gid[b] = rg;
+    sm.root_mem[b] = rm;
     uint32_t bytes = 0u;
-    if (P.tma_ok && g.len > 0) bytes = uint32_t(g.len * P.esize) & ~15u;
-    sm.bulk_elems[b] = int(bytes / uint32_t(P.esize));
-    if (bytes) {
-      const unsigned char* src = static_cast<const unsigned char*>(P.a.logits) +
-                                 (size_t(row) * size_t(P.a.ld) + size_t(g.start)) * size_t(P.esize);
-      fence_proxy_async();
-      mbar_expect_tx(&sm.full[b], bytes);
-      bulk_g2s(sm.buf[b], src, bytes, &sm.full[b]);
+    if (kind == kItemChunk || kind == kItemFollow) {
+      const Geo g = geo_of(P, row, chunk);
+      if (P.tma_ok && g.len > 0) bytes = uint32_t(g.len * P.esize) & ~15u;
+      sm.bulk_elems[b] = int(bytes / uint32_t(P.esize));
+      if (bytes) {
+        const unsigned char* src = static_cast<const unsigned char*>(P.a.logits) +
+                                   (size_t(row) * size_t(P.a.ld) + size_t(g.start)) * size_t(P.esize);
+        fence_proxy_async();
+        mbar_expect_tx(&sm.full[b], bytes);
+        bulk_g2s(sm.buf[b], src, bytes, &sm.full[b]);
+      }
     } else {
-      mbar_arrive(&sm.full[b]);
+      sm.bulk_elems[b] = 0;
     }
-    used[b] = true;
+    if (!bytes) mbar_arrive(&sm.full[b]);
+    if (kind == kItemEnd) return;
+    busy[b] = true;
     b ^= 1;
   }
 }
@@ -2209,11 +2743,14 @@ __device__ void consumer(const Params& P, Smem& sm) {
     }
     tmo = csync_or(tmo);
     fph[b] ^= 1u;
-    const long long item = sm.item[b];
-    if (item == -1) return;
-    process<T>(P, sm, b, item, tmo);
+    const int kind = sm.kind[b];
+    if (kind == kItemEnd) return;
+    const int filed = process<T>(P, sm, b, kind, tmo && kind != kItemFinish);
     csync();
-    if (threadIdx.x == 0) mbar_arrive(&sm.empty[b]);
+    if (threadIdx.x == 0) {
+      sm.mail[b] = filed;
+      mbar_arrive(&sm.empty[b]);
+    }
     b ^= 1;
   }
 }

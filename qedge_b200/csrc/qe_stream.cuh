@@ -27,7 +27,8 @@ constexpr int kMaxGroups = kMaxTiles * 32;
 constexpr int kR = 3;                         // race candidates per chunk record (filtered rows)
 constexpr int kBins = 64;                     // mass histogram bins (half a log2 unit each)
 constexpr int kSmallK = 64;                   // top-k rows up to this k gather their head
-constexpr int kGCap = 128;                    // gathered (x, id) pairs per chunk
+constexpr int kGCap = 256;                    // gathered (x, id) pairs per chunk
+constexpr int kTopM = 16;                     // group maxima per warp behind the small top-k bound
 constexpr int kTC = 4;                        // candidates per test round
 constexpr int kMaxRounds = 8;                 // follow-up rounds a row can publish
 constexpr int kQ2Cap = 256;                   // groups expanded per chunk (overflow: conservative)
@@ -38,6 +39,9 @@ constexpr uint32_t kDefaultPolls = 1u << 20;  // bound on every device-side wait
 
 enum RowKind : int { kKindGreedy = 0, kKindArgmax = 1, kKindRace = 2, kKindSmallK = 3 };
 enum RoundType : int { kRoundTest = 1, kRoundHist = 2, kRoundTies = 3, kRoundRace = 4 };
+// What the producer warp hands the compute warps in a buffer.
+enum ItemKind : int { kItemEnd = 0, kItemChunk = 1, kItemFollow = 2, kItemFinish = 3, kItemNone = 4 };
+constexpr int kFinQ = 64;                     // rows a CTA's producer has to finish (ring)
 enum : uint32_t { kFNan = 1u, kFEmpty = 2u, kFOver = 4u };
 
 // A race candidate: ratio in the producing chunk's scale, logit, noise, id.
@@ -102,19 +106,24 @@ struct HistAcc {
   unsigned int pad[3];
 };
 
-// Launch-wide counters, zeroed before every launch.
-struct alignas(16) Ctl {
-  unsigned int next;         // chunk items claimed
+// Launch-wide counters, zeroed before every launch; each on its own 128-byte
+// line so that polling one does not queue behind atomics on another.
+struct alignas(128) Ctl {
   unsigned int qentries;     // follow-up rounds published
+  unsigned int pad0[31];
   unsigned int qhead;        // follow-up items claimed
+  unsigned int pad1[31];
   unsigned int rows_done;
+  unsigned int pad2[31];
   unsigned int err;          // 1: a bounded wait gave up
-  unsigned int pad[3];
+  unsigned int pad3[31];
 };
 
 struct RowCtl {
   unsigned int cnt;          // arrivals in the row's current round
   unsigned int timeout;      // a wait on one of the row's chunks gave up
+  unsigned int round;        // the row's current round: 0 = chunk records, else RoundType
+  unsigned int pad;
 };
 
 // Workspace layout (offsets in bytes from the workspace base).
