@@ -20,13 +20,16 @@ noise for tokens that cannot win the race:
 
 * root (one per row): ``E_root = -ln(u_root) / V``; a uniformly chosen token
   ``s`` carries that minimum;
-* group ``G`` (up to 32 tokens, layout below), one Philox call whose counter
-  is the global group id, words ``(x, y, z, w)``:
-  ``E_min(G) = E_root + (-ln(u_x)) / n_G`` carried by member
-  ``select(y, n_G)`` -- or ``E_root`` carried by ``s`` if ``s`` is in ``G``;
-  then the second smallest value ``E2(G) = E_min(G) + (-ln(u_z)) / (n_G - 1)``
-  carried by member ``select(w, n_G - 1)`` counted among the members other
-  than the argmin;
+* group ``G`` (up to 32 tokens, layout below, global group id ``g``): its
+  minimum ``E_min(G) = E_root + (-ln(u_m)) / n_G`` where ``u_m`` is word
+  ``g mod 4`` of one Philox call with counter ``g // 4`` (tag 3: one call
+  serves four consecutive groups, so the kernel can bound every group cheaply),
+  carried by member ``select(y, n_G)`` -- or ``E_root`` carried by ``s`` if
+  ``s`` is in ``G``; then the second smallest value
+  ``E2(G) = E_min(G) + (-ln(u_z)) / (n_G - 1)`` carried by member
+  ``select(w, n_G - 1)`` counted among the members other than the argmin,
+  where ``(y, z, w)`` are words of one Philox call whose counter is ``g``
+  (tag 1; word ``x`` is unused);
 * every other token ``j`` of ``G``: ``E_j = E2(G) + (-ln(u_j))``.
 
 By the memoryless property of the exponential distribution this is exactly
@@ -45,7 +48,7 @@ PHILOX_M1 = 0xCD9E8D57
 PHILOX_W0 = 0x9E3779B9
 PHILOX_W1 = 0xBB67AE85
 
-TAG_ROOT, TAG_GROUP, TAG_TOKEN = 0, 1, 2
+TAG_ROOT, TAG_GROUP, TAG_TOKEN, TAG_GMIN = 0, 1, 2, 3
 NSLICE = 16         # canonical vocab slices per row (also the max vocab-shard count)
 TILE = 1024         # ids per tile inside a slice
 GROUP_LANES = 32    # groups per tile
@@ -203,7 +206,9 @@ def philox_noise(B: int, V: int, seed: int, step: int, row_offset: int = 0) -> n
         e_root = (neglog_f32(uniform_open(w[0])) / Vf).astype(np.float32)
         s = int(_select(w[1], w[2], V))
         wg = philox4x32_10(garange, row, s_lo, hi | TAG_GROUP, k0, k1)
-        e_min = (e_root + (neglog_f32(uniform_open(wg[0])) / nf).astype(np.float32)).astype(np.float32)
+        wq = philox4x32_10(garange >> 2, row, s_lo, hi | TAG_GMIN, k0, k1)
+        umin = np.choose((garange & 3).astype(np.int64), wq)
+        e_min = (e_root + (neglog_f32(uniform_open(umin)) / nf).astype(np.float32)).astype(np.float32)
         arg = _select32(wg[1], n)
         gs = gid[s]
         e_min[gs] = e_root

@@ -111,7 +111,7 @@ __device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
   }
   return c;
 }
-enum : uint32_t { kTagRoot = 0, kTagGroup = 1, kTagToken = 2 };
+enum : uint32_t { kTagRoot = 0, kTagGroup = 1, kTagToken = 2, kTagGroupMin = 3 };
 
 // Odd multiple of 2^-24 in (0,1): exact in fp32.
 __device__ __forceinline__ float uniform_open(uint32_t w) {
@@ -177,23 +177,32 @@ __device__ __forceinline__ NoiseRoot noise_root(const NoiseKey& k, int64_t V) {
   r.s = select_index(w.y, w.z, uint32_t(V));
   return r;
 }
-// Noise of a group of n members (one Philox call, counter = global group
-// id): its minimum E_min and the member carrying it, then the gap to the
-// second smallest value, E2 = E_min + (-ln u')/(n-1), and the member
-// carrying that (uniform among the others).  Every other member j has
-// E_j = E2 + (-ln u_j).  Words: x -> E_min, y -> argmin, z -> E2, w -> the
-// second member.  The group holding the root token s takes E_min = E_root
-// with s as its argmin.
+__device__ __forceinline__ uint32_t pick_word(const U4& w, uint32_t i) {
+  return i == 0u ? w.x : i == 1u ? w.y : i == 2u ? w.z : w.w;
+}
+// Word of group gid's noise minimum: one Philox call (tag kTagGroupMin,
+// counter gid / 4) covers four consecutive groups, word gid % 4 each, so a
+// kernel can bound every group's best ratio at a quarter of the cost.
+__device__ __forceinline__ uint32_t group_min_word(const NoiseKey& k, int64_t gid) {
+  return pick_word(philox_at(k, uint32_t(gid >> 2), kTagGroupMin), uint32_t(gid & 3));
+}
+// Noise of a group of n members: its minimum E_min = E_root + (-ln u)/n
+// (u from group_min_word) and, from one Philox call with counter = global
+// group id (tag kTagGroup), the member carrying it (word y), the gap to the
+// second smallest value, E2 = E_min + (-ln u')/(n-1) (word z), and the
+// member carrying that, uniform among the others (word w).  Every other
+// member j has E_j = E2 + (-ln u_j).  The group holding the root token s
+// takes E_min = E_root with s as its argmin.
 struct GroupNoise { float e_min, e2; int arg, arg2; };
-__device__ __forceinline__ GroupNoise group_noise_from(const NoiseRoot& root, U4 w, int n, bool holds_root,
-                                                       int mem_s) {
+__device__ __forceinline__ GroupNoise group_noise_from(const NoiseRoot& root, U4 w, uint32_t wmin, int n,
+                                                       bool holds_root, int mem_s) {
   GroupNoise g;
   if (holds_root) {
     g.e_min = root.e_root;
     g.arg = mem_s;
   } else {
     // n = 32 (every full group): the division is an exact scaling by 2^-5
-    const float l = neglog(uniform_open(w.x));
+    const float l = neglog(uniform_open(wmin));
     g.e_min = __fadd_rn(root.e_root, n == 32 ? __fmul_rn(l, 0.03125f) : __fdiv_rn(l, float(n)));
     g.arg = int(select_index32(w.y, uint32_t(n)));
   }
@@ -209,15 +218,14 @@ __device__ __forceinline__ GroupNoise group_noise_from(const NoiseRoot& root, U4
 }
 __device__ __forceinline__ GroupNoise noise_group(const NoiseKey& k, const NoiseRoot& root, int64_t gid, int n,
                                                   int64_t gid_s, int mem_s) {
-  return group_noise_from(root, philox_at(k, uint32_t(gid), kTagGroup), n, gid == gid_s, mem_s);
+  return group_noise_from(root, philox_at(k, uint32_t(gid), kTagGroup), group_min_word(k, gid), n, gid == gid_s,
+                          mem_s);
 }
 // Noise of token j (global id) that is member `mem` of group g.
 __device__ __forceinline__ float noise_token(const NoiseKey& k, const GroupNoise& g, int64_t j, int mem) {
   if (mem == g.arg) return g.e_min;
   if (mem == g.arg2) return g.e2;
-  U4 w = philox_at(k, uint32_t(j >> 2), kTagToken);
-  uint32_t word = (j & 3) == 0 ? w.x : (j & 3) == 1 ? w.y : (j & 3) == 2 ? w.z : w.w;
-  return __fadd_rn(g.e2, neglog(uniform_open(word)));
+  return __fadd_rn(g.e2, neglog(uniform_open(pick_word(philox_at(k, uint32_t(j >> 2), kTagToken), uint32_t(j & 3)))));
 }
 
 // Global group id of token j in a row of V ids, plus its member index.
