@@ -34,6 +34,11 @@ Extensions the reference does not have (parity pinned by this oracle only):
   same stable order; the top-p mass is measured on the full distribution.
   Rows with an active ``top_k`` take the sorted path even when
   ``use_top_p`` is False.
+* ``min_p`` (``SamplingParams.min_p``, packed by ``src/data/batch.py:60, 158``
+  but never applied by the reference sampler): ``remove |= p < RN(min_p *
+  p_max)`` in the same stable order (``p_max`` is the row's largest
+  probability), so min-p, like top-k, removes a suffix of that order.  Rows
+  with ``min_p > 0`` take the sorted path even when ``use_top_p`` is False.
 * repetition penalty over the set of ids in the row's history, applied to
   ``logits.float()`` before temperature: ``x = x * rp if x < 0 else x / rp``
   (the rule of the Hugging Face repetition-penalty processor).  Greedy rows
@@ -103,7 +108,7 @@ def softmax_f32(y: np.ndarray) -> np.ndarray:
 
 
 def sample_row(x: np.ndarray, T: float, top_p: float, top_k: int, noise: np.ndarray,
-               *, use_top_p: bool, all_greedy: bool = False) -> RowResult:
+               *, use_top_p: bool, all_greedy: bool = False, min_p: float = 0.0) -> RowResult:
     """One row of the reference sampler on penalised float32 logits ``x``."""
     V = x.shape[0]
     if all_greedy or np.float32(T) <= GREEDY_EPS:
@@ -114,7 +119,8 @@ def sample_row(x: np.ndarray, T: float, top_p: float, top_k: int, noise: np.ndar
     if not np.all(np.isfinite(p)):
         return RowResult(_argmax_first(x), True, 0)
     k_active = 0 < top_k < V
-    if use_top_p or k_active:
+    m_active = np.float32(min_p) > 0
+    if use_top_p or k_active or m_active:
         order = np.argsort(-p, kind="stable")
         vals = p[order]
         remove = np.zeros(V, dtype=bool)
@@ -123,6 +129,8 @@ def sample_row(x: np.ndarray, T: float, top_p: float, top_k: int, noise: np.ndar
             remove |= (cs - vals).astype(np.float32) > np.float32(top_p)
         if k_active:
             remove[top_k:] = True
+        if m_active:
+            remove |= vals < np.float32(np.float32(min_p) * vals[0])
         vals = np.where(remove, np.float32(0), vals)
         with np.errstate(divide="ignore", invalid="ignore"):
             r = (vals / noise[order]).astype(np.float32)
@@ -135,7 +143,8 @@ def sample_row(x: np.ndarray, T: float, top_p: float, top_k: int, noise: np.ndar
 
 def sample(logits: np.ndarray, temperatures, top_ps, noise: np.ndarray, *,
            top_ks=None, rep_penalties=None, history=None, history_lens=None,
-           all_greedy: bool = False, use_top_p: bool = False, details: bool = False):
+           all_greedy: bool = False, use_top_p: bool = False, details: bool = False,
+           min_ps=None):
     """Batch restatement of ``BatchSampler.forward`` with the extensions.
 
     ``logits`` is float32 ``[B, V]`` (convert bf16/fp16 inputs first, exactly
@@ -148,6 +157,7 @@ def sample(logits: np.ndarray, temperatures, top_ps, noise: np.ndarray, *,
     tps = np.ones(B, np.float32) if top_ps is None else np.asarray(top_ps, dtype=np.float32).reshape(B)
     tks = np.zeros(B, np.int64) if top_ks is None else np.asarray(top_ks, dtype=np.int64).reshape(B)
     rps = np.ones(B, np.float32) if rep_penalties is None else np.asarray(rep_penalties, dtype=np.float32).reshape(B)
+    mps = np.zeros(B, np.float32) if min_ps is None else np.asarray(min_ps, dtype=np.float32).reshape(B)
     out = np.empty(B, dtype=np.int64)
     rows = []
     for b in range(B):
@@ -157,7 +167,7 @@ def sample(logits: np.ndarray, temperatures, top_ps, noise: np.ndarray, *,
             h = history[b, :n]
         x = penalise(logits[b], h, float(rps[b]))
         res = sample_row(x, float(temps[b]), float(tps[b]), int(tks[b]), noise[b],
-                         use_top_p=use_top_p, all_greedy=all_greedy)
+                         use_top_p=use_top_p, all_greedy=all_greedy, min_p=float(mps[b]))
         out[b] = res.token
         rows.append(res)
     return (out, rows) if details else out

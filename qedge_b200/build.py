@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -43,14 +44,17 @@ def build(verbose: bool = False, extra=(), force: bool = False) -> Path:
     deps = srcs + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "qedge_sample.h"]
     if not force and LIB.exists() and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in deps) and not extra:
         return LIB
-    objs = []
-    for s in srcs:
-        o = OUT_DIR / (s.stem + ".o")
-        cmd = [nvcc(), *flags(extra), "-dc" if False else "-c", str(s), "-o", str(o)]
-        if verbose:
-            print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
-        objs.append(str(o))
+    objs = [str(OUT_DIR / (src.stem + ".o")) for src in srcs]
+    cmds = [[nvcc(), *flags(extra), "-c", str(src), "-o", o] for src, o in zip(srcs, objs)]
+    if verbose:
+        for c in cmds:
+            print(" ".join(c))
+    # translation units compile in parallel (ptxas dominates)
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for r in list(ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), cmds)):
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout + r.stderr)
+                raise subprocess.CalledProcessError(r.returncode, r.args)
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs, "-cudart", "static"]
     if verbose:

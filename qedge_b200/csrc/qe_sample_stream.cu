@@ -1,5 +1,5 @@
-// qe_sample_stream.cu — the default sampler path: two launches, the logits
-// read from HBM once.
+// qe_sample_stream.cu — the default sampler path: the logits read from HBM
+// once, four launches.
 //
 // Replaces BatchSampler.forward (src/compute/sampler.py:25-41) and the
 // extensions of this library (top-k, min-p, repetition penalty, Philox
@@ -8,26 +8,25 @@
 // prefix of the order (x desc, id asc) allowed by top-k, top-p and min-p,
 // token = argmax over the kept set of rho = RN(RN(e/S)/E).
 //
-// 1. summ_kernel streams the logits: one warp per task of `tpw` tiles (4 KB
-//    of logits), each lane one 32-id group at a time held in registers
-//    (16-byte loads), reduced to (max, group-relative exponential sum).  No
-//    barriers, no shared memory beyond the penalty bits, so enough warps are
-//    resident to keep HBM busy.
-// 2. row_kernel, one CTA per row, works from the row's group summaries
-//    (8 bytes per 32 ids, still in L2):
+// 1. scan_kernel streams the logits: one warp per task of `tpw` tiles (4 KB
+//    of bf16 logits per pair of tiles), each lane one 32-id group at a time
+//    held in registers (16-byte loads), reduced to a GroupSum (max,
+//    group-relative exponential sum); per task a TaskRec: max, sum in the
+//    task's scale, and the two largest group noise bounds with a ceiling for
+//    the rest (one Philox call per four groups).  No barriers.
+// 2. decide_kernel, one CTA per row, from the task records (still in L2):
 //      * row max, softmax normaliser S, greedy / top-1 / non-finite rows;
-//      * the exponential race: every group's best ratio is bounded by its
-//        largest term over its noise minimum (one Philox call per four
-//        groups); only groups whose bound reaches 1/16 (the 4th best ratio
-//        of a race is below that with probability ~1e-4) are re-read and
-//        raced exactly, and the 4 best are complete above that threshold;
-//      * the kept-set test of those candidates: bounded from the summaries,
-//        or counted exactly over the groups whose max is at or above them;
-//      * top-k rows with k <= 64: the k-th largest group max bounds the
-//        k-th largest logit, so only those groups are read, sorted and raced;
-//      * the exact fallback (candidates all outside the kept set, or the
-//        kept-set size asked for): radix rounds over the keys of the groups
-//        at or above a floor, the tie rank, and the race over the kept set.
+//      * the exponential race over the groups whose bound reaches 1/4 (the
+//        best ratio of a race is below that with probability e^-4), then
+//        1/64: one group per thread, re-read and raced exactly;
+//      * the kept-set test of the 4 best candidates from the task records,
+//        then from the group records of the tasks that can hold ids ahead.
+// 3. count_kernel counts exactly, over all SMs, the ids ahead of the
+//    candidates of the rows the records could not settle; the warp that
+//    completes a row decides it (no waiting on other CTAs).
+// 4. finish_kernel (persistent CTAs) takes the rest: top-k rows with
+//    k <= 64 (the k largest, sorted) and the exact fallback (radix rounds
+//    over the keys, the tie rank, the race over the kept set).
 // No kernel waits for another CTA or on any flag.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -72,18 +71,22 @@ struct Params {
   int esize;                    // bytes per logit
   int vec_ok;                   // 16-byte loads of logits
   int noise_vec;                // 16-byte loads of caller noise
-  int tpw;                      // tiles per warp task (2 for 16-bit types, 1 for fp32)
-  int tasks_row;                // warp tasks per row
+  int tpw;                      // tiles per scan task
+  int tasks_row;                // scan tasks per row
   int force_exact;              // the kept-set size is asked for
   int dtype_level;              // last radix level that separates the dtype's values
   int64_t G;                    // groups per row
   int64_t sstart[kNumSlices + 1];
   int64_t gbase[kNumSlices + 1];
   int snt[kNumSlices];          // tiles per slice
-  int tbase[kNumSlices + 1];    // first warp task of each slice
+  int tbase[kNumSlices + 1];    // first scan task of each slice
   Ctl* ctl;
   GroupSum* summ;               // [B][G]
+  TaskRec* trec;                // [B][tasks_row]
   float* emin;                  // [B][G] noise minimum per group (caller-noise mode)
+  RowState* rstate;             // [B]
+  int* plist;                   // rows queued for the count kernel
+  int* flist;                   // rows queued for the finish kernel (row | kind << 28)
 };
 
 // ---------------------------------------------------------------- row parameters
@@ -264,11 +267,69 @@ __device__ __forceinline__ int first_member_packed(const uint32_t w[16], float v
   return f;
 }
 
-// ---------------------------------------------------------------- 1. summaries
+
+// ---------------------------------------------------------------- 1. scan
+// Penalty bits of up to two tiles of a slice: bit (b*8+i) of word tt*32+l
+// is set when slice offset (tile0+tt)*1024 + b*256 + l*8 + i is in the
+// history.  Warp-local; the caller's warp runs it together.
+__device__ __forceinline__ void pen_bits_build(uint32_t* bits, const int32_t* hist, int hl, int64_t sa, int tile0,
+                                               int nt, int L) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  bits[lane] = 0u;
+  bits[lane + 32] = 0u;
+  __syncwarp();
+  const int64_t base = int64_t(tile0) * kTile;
+  for (int h = lane; h < hl; h += 32) {
+    const int64_t o = int64_t(hist[h]) - sa - base;
+    if (o >= 0 && o < int64_t(nt) * kTile && base + o < L)
+      atomicOr(&bits[(o >> 10) * 32 + ((o >> 3) & 31)], 1u << int(((o >> 8) & 3) * 8 + (o & 7)));
+  }
+  __syncwarp();
+}
+
+// Lower bound of a group's noise minimum in Philox mode without the tree's
+// root: E_min = E_root + (-ln u)/n >= (-ln u)/32.  The approximate log is
+// pulled down by more than its error, so the bound holds; the group holding
+// the root token is added to every race by the decide kernel instead.
+__device__ __forceinline__ float emin_lower(uint32_t wmin) {
+  const float la = -lg2_approx(uniform_open(wmin)) * 0.6931472f;
+  return fmaxf(0.f, la * (1.f - 3e-5f) - 3e-5f) * 0.03125f * (1.f - 2e-6f);
+}
+
+// A lane's three largest bound keys (group ids kept for the first two).
+struct Top3 {
+  float b0, b1, b2;
+  int g0, g1;
+  __device__ __forceinline__ void init() {
+    b0 = b1 = b2 = -INFINITY;
+    g0 = g1 = -1;
+  }
+  __device__ __forceinline__ void add(float k, int g) {
+    if (!(k > b2)) return;
+    if (k > b1) {
+      b2 = b1;
+      if (k > b0) {
+        b1 = b0; g1 = g0;
+        b0 = k; g0 = g;
+      } else {
+        b1 = k; g1 = g;
+      }
+    } else {
+      b2 = k;
+    }
+  }
+};
+
 template <typename T>
-__global__ void __launch_bounds__(kSumThreads, 3) summ_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_constant__ Params P) {
   __shared__ uint32_t pen_bits[kSumThreads / 32][64];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    P.ctl->err = 0u;
+    P.ctl->n_pend = 0u;
+    P.ctl->n_fin = 0u;
+  }
   const long long task = (long long)blockIdx.x * (blockDim.x >> 5) + wib;
   if (task >= (long long)P.a.batch * P.tasks_row) return;   // the whole warp
   const int row = int(task / P.tasks_row), t = int(task % P.tasks_row);
@@ -276,6 +337,7 @@ __global__ void __launch_bounds__(kSumThreads, 3) summ_kernel(const __grid_const
 #pragma unroll 1
   while (s + 1 < kNumSlices && P.tbase[s + 1] <= t) ++s;
   const int tile0 = (t - P.tbase[s]) * P.tpw;
+  const int ntile = min(P.tpw, P.snt[s] - tile0);
   const int64_t sa = P.sstart[s];
   const int L = int(P.sstart[s + 1] - sa);
   const KernelArgs& a = P.a;
@@ -291,112 +353,173 @@ __global__ void __launch_bounds__(kSumThreads, 3) summ_kernel(const __grid_const
     hl = hl < 0 ? 0 : (hl > int(a.history_ld) ? int(a.history_ld) : hl);
   }
   const bool pen = hl > 0 && !(rpen == 1.f);
-  if (pen) {
-    pen_bits[wib][lane] = 0u;
-    pen_bits[wib][lane + 32] = 0u;
-    __syncwarp();
-    const int32_t* hist = a.history + row * a.history_ld;
-    const int64_t base = int64_t(tile0) * kTile;   // slice offset of the task's first id
-    for (int h = lane; h < hl; h += 32) {
-      const int64_t o = int64_t(hist[h]) - sa - base;
-      if (o >= 0 && o < int64_t(P.tpw) * kTile && base + o < L)
-        atomicOr(&pen_bits[wib][(o >> 10) * 32 + ((o >> 3) & 31)], 1u << int(((o >> 8) & 3) * 8 + (o & 7)));
-    }
-    __syncwarp();
-  }
+  const int32_t* hist = pen ? a.history + row * a.history_ld : nullptr;
+  const NoiseKey key = make_noise_key(row_seed(a, row), a.step_ptr ? *a.step_ptr : a.step, a.row_offset + row);
   const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
-  GroupSum* out = P.summ + size_t(row) * size_t(P.G) + size_t(P.gbase[s]);
-  // 16-bit types: both tiles' loads in flight before any arithmetic
-  uint32_t wv[2][16];
-  bool fast[2] = {false, false};
-  if constexpr (sizeof(T) == 2) {
+  const int64_t g_first = P.gbase[s] + int64_t(tile0) * 32;   // global id of the task's first group
+  GroupSum* out = P.summ + size_t(row) * size_t(P.G) + size_t(g_first);
+  const float* nzrow = a.noise ? a.noise + size_t(row) * size_t(a.noise_ld) + size_t(sa) : nullptr;
+  // per-lane task state: NaN-aware max, sum in the lane's running scale, bound keys
+  float lmax = -INFINITY, lu = -INFINITY;
+  double lsum = 0.0;
+  Top3 top;
+  top.init();
+  constexpr int kStep = sizeof(T) == 2 ? 2 : 1;   // tiles per load round
+#pragma unroll 1
+  for (int tp = 0; tp < ntile; tp += kStep) {
+    const int nt = min(kStep, ntile - tp);
+    const int tbase = tile0 + tp;
+    if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tbase, nt, L);
+    // 16-bit rows: every full tile's loads in flight before any arithmetic
+    uint32_t wv[2][16];
+    bool fast[2] = {false, false};
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        const int tile = tbase + tt;
+        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
+        fast[tt] = tt < nt && pb == 0u && tile * kTile + kTile <= L && P.vec_ok;
+        if (fast[tt]) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + size_t(tile * kTile + b * 256 + lane * 8) * 2));
+            wv[tt][4 * b] = q.x; wv[tt][4 * b + 1] = q.y; wv[tt][4 * b + 2] = q.z; wv[tt][4 * b + 3] = q.w;
+          }
+        }
+      }
+    }
+    // group-minimum noise words of the round's groups (one Philox call per four)
+    uint32_t wmin[2] = {0u, 0u};
+    if (!idx_mode && !a.noise) {
+      U4 w{0u, 0u, 0u, 0u};
+      const int64_t gq = (g_first + int64_t(tp) * 32) >> 2;   // the round's groups start at a multiple of 32
+      if (lane < nt * 8) w = philox_at(key, uint32_t(gq + lane), kTagGroupMin);
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        const int srcl = tt * 8 + (lane >> 2);
+        const U4 v{__shfl_sync(0xFFFFFFFFu, w.x, srcl), __shfl_sync(0xFFFFFFFFu, w.y, srcl),
+                   __shfl_sync(0xFFFFFFFFu, w.z, srcl), __shfl_sync(0xFFFFFFFFu, w.w, srcl)};
+        wmin[tt] = pick_word(v, uint32_t(lane & 3));
+      }
+    }
 #pragma unroll
     for (int tt = 0; tt < 2; ++tt) {
-      const int tile = tile0 + tt;
-      const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
-      fast[tt] = tt < P.tpw && tile < P.snt[s] && pb == 0u && tile * kTile + kTile <= L && P.vec_ok;
-      if (fast[tt]) {
+      if (tt >= nt) break;
+      const int tile = tbase + tt;
+      GroupSum r;
+      bool done = false;
+      if constexpr (sizeof(T) == 2) {
+        if (fast[tt]) {
+          done = true;
+          const uint32_t* w = wv[tt];
+          const uint32_t m0 = Cvt<T>::max2(Cvt<T>::max2(w[0], w[1]), Cvt<T>::max2(w[2], w[3]));
+          const uint32_t m1 = Cvt<T>::max2(Cvt<T>::max2(w[4], w[5]), Cvt<T>::max2(w[6], w[7]));
+          const uint32_t m2 = Cvt<T>::max2(Cvt<T>::max2(w[8], w[9]), Cvt<T>::max2(w[10], w[11]));
+          const uint32_t m3 = Cvt<T>::max2(Cvt<T>::max2(w[12], w[13]), Cvt<T>::max2(w[14], w[15]));
+          const uint32_t mm = Cvt<T>::max2(Cvt<T>::max2(m0, m1), Cvt<T>::max2(m2, m3));
+          const float lo = Cvt<T>::lo(mm), hi = Cvt<T>::hi(mm);
+          const float gmax = (lo != lo || hi != hi) ? __int_as_float(0x7FFFFFFF) : fmaxf(lo, hi);
+          r.gmax = gmax;
+          if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
+            r.aux = __int_as_float(first_member_packed<T>(w, gmax));
+          else
+            r.aux = gmax > -INFINITY ? group_sum_packed<T>(w, c1, -__fmul_rn(gmax, c1)) : 0.f;
+        }
+      }
+      if (!done) {
+        float x[32];
+        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
+        load_members<T>(P, src, tile, lane, L, x);
+        if (pb) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m)
+            if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
+        }
+        float gmax = x[0];
+#pragma unroll
+        for (int m = 1; m < 32; ++m) gmax = fmax_nan(gmax, x[m]);
+        r.gmax = gmax;
+        // rows that only need the max's position, and groups whose softmax terms
+        // are not finite (the row then falls back to the greedy id), keep the
+        // position of the group's max instead of its sum
+        if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
+          r.aux = __int_as_float(first_member(x, gmax));
+        else
+          r.aux = gmax > -INFINITY ? group_sum(x, c1, -__fmul_rn(gmax, c1)) : 0.f;
+      }
+      const int64_t gl = int64_t(tp + tt) * 32 + lane;   // group index inside the task
+      out[gl] = r;
+      lmax = fmax_nan(lmax, r.gmax);
+      if (idx_mode || !(r.gmax > -INFINITY) || !finite_f(__fmul_rn(r.gmax, c1))) continue;
+      // the group's lower bound of its noise minimum
+      float lo;
+      if (nzrow) {
+        float e = INFINITY;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + size_t(tile * kTile + b * 256 + lane * 8) * 2));
-          wv[tt][4 * b] = q.x; wv[tt][4 * b + 1] = q.y; wv[tt][4 * b + 2] = q.z; wv[tt][4 * b + 3] = q.w;
+          const int off = tile * kTile + b * 256 + lane * 8;
+          const int nb = L - off;
+          if (nb >= 8 && P.noise_vec) {
+            const float4 q0 = __ldg(reinterpret_cast<const float4*>(nzrow + off));
+            const float4 q1 = __ldg(reinterpret_cast<const float4*>(nzrow + off + 4));
+            e = fminf(e, fminf(fminf(fminf(q0.x, q0.y), fminf(q0.z, q0.w)), fminf(fminf(q1.x, q1.y), fminf(q1.z, q1.w))));
+          } else {
+            for (int i = 0; i < 8 && i < nb; ++i) e = fminf(e, __ldg(nzrow + off + i));
+          }
         }
+        P.emin[size_t(row) * size_t(P.G) + size_t(g_first + gl)] = e;
+        lo = e;
+      } else {
+        lo = emin_lower(wmin[tt]);
       }
+      const float ug = __fmul_rn(r.gmax, c1);
+      if (ug > lu) {
+        lsum = lsum * double(qe_ex2_ftz(__fsub_rn(lu, ug))) + double(r.aux);
+        lu = ug;
+      } else {
+        lsum += double(r.aux) * double(qe_ex2_ftz(__fsub_rn(ug, lu)));
+      }
+      top.add(lo > 0.f ? ug - lg2_approx(lo) : INFINITY, int(g_first + gl));
     }
   }
+  // task record: warp reductions
+  const uint32_t kmax = __reduce_max_sync(0xFFFFFFFFu, nan_key(lmax));
+  const float tmax = kmax == 0xFFFFFFFFu ? __int_as_float(0x7FFFFFFF) : key_to_float(kmax);
+  TaskRec tr;
+  tr.tmax = tmax;
+  double ts = 0.0;
+  if (!idx_mode) {
+    const float ut = __fmul_rn(tmax, c1);
+    if (lu > -INFINITY && finite_f(ut)) ts = lsum * double(qe_ex2_ftz(__fsub_rn(lu, ut)));
 #pragma unroll
-  for (int tt = 0; tt < 2; ++tt) {
-    if (tt >= P.tpw) break;
-    const int tile = tile0 + tt;
-    if (tile >= P.snt[s]) break;
-    GroupSum r;
-    bool done = false;
-    if constexpr (sizeof(T) == 2) {
-     if (fast[tt]) {
-      done = true;
-      const uint32_t* w = wv[tt];
-      const uint32_t m0 = Cvt<T>::max2(Cvt<T>::max2(w[0], w[1]), Cvt<T>::max2(w[2], w[3]));
-      const uint32_t m1 = Cvt<T>::max2(Cvt<T>::max2(w[4], w[5]), Cvt<T>::max2(w[6], w[7]));
-      const uint32_t m2 = Cvt<T>::max2(Cvt<T>::max2(w[8], w[9]), Cvt<T>::max2(w[10], w[11]));
-      const uint32_t m3 = Cvt<T>::max2(Cvt<T>::max2(w[12], w[13]), Cvt<T>::max2(w[14], w[15]));
-      const uint32_t mm = Cvt<T>::max2(Cvt<T>::max2(m0, m1), Cvt<T>::max2(m2, m3));
-      const float lo = Cvt<T>::lo(mm), hi = Cvt<T>::hi(mm);
-      const float gmax = (lo != lo || hi != hi) ? __int_as_float(0x7FFFFFFF) : fmaxf(lo, hi);
-      r.gmax = gmax;
-      if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
-        r.aux = __int_as_float(first_member_packed<T>(w, gmax));
-      else
-        r.aux = gmax > -INFINITY ? group_sum_packed<T>(w, c1, -__fmul_rn(gmax, c1)) : 0.f;
-     }
-    }
-    if (!done) {
-      float x[32];
-      const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
-      load_members<T>(P, src, tile, lane, L, x);
-      if (pb) {
-#pragma unroll
-        for (int m = 0; m < 32; ++m)
-          if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
-      }
-      float gmax = x[0];
-#pragma unroll
-      for (int m = 1; m < 32; ++m) gmax = fmax_nan(gmax, x[m]);
-      r.gmax = gmax;
-      // rows that only need the max's position, and groups whose softmax terms
-      // are not finite (the row then falls back to the greedy id), keep the
-      // position of the group's max instead of its sum
-      if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
-        r.aux = __int_as_float(first_member(x, gmax));
-      else
-        r.aux = gmax > -INFINITY ? group_sum(x, c1, -__fmul_rn(gmax, c1)) : 0.f;
-    }
-    out[tile * 32 + lane] = r;
-    if (a.noise && !idx_mode) {
-      // caller-noise mode: the group's smallest noise bounds its best ratio
-      const float* nz = a.noise + size_t(row) * size_t(a.noise_ld) + size_t(sa);
-      float e = INFINITY;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int off = tile * kTile + b * 256 + lane * 8;
-        const int nb = L - off;
-        if (nb >= 8 && P.noise_vec) {
-          const float4 q0 = __ldg(reinterpret_cast<const float4*>(nz + off));
-          const float4 q1 = __ldg(reinterpret_cast<const float4*>(nz + off + 4));
-          e = fminf(e, fminf(fminf(fminf(q0.x, q0.y), fminf(q0.z, q0.w)), fminf(fminf(q1.x, q1.y), fminf(q1.z, q1.w))));
-        } else {
-          for (int i = 0; i < 8 && i < nb; ++i) e = fminf(e, __ldg(nz + off + i));
-        }
-      }
-      P.emin[size_t(row) * size_t(P.G) + size_t(P.gbase[s]) + size_t(tile * 32 + lane)] = e;
-    }
+    for (int o = 16; o > 0; o >>= 1) ts += __shfl_xor_sync(0xFFFFFFFFu, ts, o);
   }
+  tr.tsum = ts;
+  float kv[3];
+  int kg[2];
+  int h = 0;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float hv = h == 0 ? top.b0 : h == 1 ? top.b1 : h == 2 ? top.b2 : -INFINITY;
+    const int hg = h == 0 ? top.g0 : h == 1 ? top.g1 : -1;
+    const uint32_t kk = ordered_key(hv);
+    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kk);
+    const int srcl = __ffs(__ballot_sync(0xFFFFFFFFu, kk == km)) - 1;
+    kv[i] = __shfl_sync(0xFFFFFFFFu, hv, srcl);
+    if (i < 2) kg[i] = __shfl_sync(0xFFFFFFFFu, hg, srcl);
+    if (lane == srcl) ++h;
+  }
+  tr.bk0 = kv[0];
+  tr.bk1 = kv[1];
+  tr.bceil = kv[2];
+  tr.bg0 = kv[0] > -INFINITY ? kg[0] : -1;
+  tr.bg1 = kv[1] > -INFINITY ? kg[1] : -1;
+  if (lane == 0) P.trec[size_t(row) * size_t(P.tasks_row) + size_t(t)] = tr;
 }
 
+
+// ---------------------------------------------------------------- shared row helpers
 // ---------------------------------------------------------------- 2. row kernel: shared state
-struct Cand {
-  float r, x, E;
-  int id;
-};
 
 // The kTC best (rho desc, id asc) one thread has seen.
 struct Top4 {
@@ -530,8 +653,8 @@ __device__ __forceinline__ void block_sum4(RowSm& sm, double* ms, long long* ct)
 
 // ---------------------------------------------------------------- history hash (repetition penalty)
 __device__ __forceinline__ uint32_t hslot(int id) { return (uint32_t(id) * 2654435761u) >> 19; }   // 13 bits
-__device__ __forceinline__ void hash_build(RowSm& sm, const RowP& rp, int64_t V) {
-  for (int i = threadIdx.x; i < kHashCap; i += kRowThreads) sm.hash[i] = -1;
+__device__ __forceinline__ void hash_build(int* hash, const RowP& rp, int64_t V) {
+  for (int i = threadIdx.x; i < kHashCap; i += kRowThreads) hash[i] = -1;
   __syncthreads();
   if (rp.hash_ok) {
     for (int h = threadIdx.x; h < rp.hlen; h += kRowThreads) {
@@ -540,7 +663,7 @@ __device__ __forceinline__ void hash_build(RowSm& sm, const RowP& rp, int64_t V)
       uint32_t s = hslot(id);
 #pragma unroll 1
       for (int probe = 0; probe < kHashCap; ++probe) {
-        const int prev = atomicCAS(&sm.hash[s], -1, id);
+        const int prev = atomicCAS(&hash[s], -1, id);
         if (prev == -1 || prev == id) break;
         s = (s + 1u) & uint32_t(kHashCap - 1);
       }
@@ -548,12 +671,12 @@ __device__ __forceinline__ void hash_build(RowSm& sm, const RowP& rp, int64_t V)
   }
   __syncthreads();
 }
-__device__ __forceinline__ bool in_history(const RowSm& sm, const RowP& rp, int id) {
+__device__ __forceinline__ bool in_history(const int* hash, const RowP& rp, int id) {
   if (rp.hash_ok) {
     uint32_t s = hslot(id);
 #pragma unroll 1
     for (int probe = 0; probe < kHashCap; ++probe) {
-      const int v = sm.hash[s];
+      const int v = hash[s];
       if (v == id) return true;
       if (v == -1) return false;
       s = (s + 1u) & uint32_t(kHashCap - 1);
@@ -610,7 +733,7 @@ __device__ __forceinline__ void lane_visit(const Params& P, RowSm& sm, const Row
       const int bid = int(q.base) + (q.lg >> 5) * kTile + (q.lg & 31) * 8;
 #pragma unroll
       for (int m = 0; m < 32; ++m)
-        if (m < q.n && in_history(sm, rp, bid + (m >> 3) * 256 + (m & 7))) x[m] = pen_x(x[m], rp.rp);
+        if (m < q.n && in_history(sm.hash, rp, bid + (m >> 3) * 256 + (m & 7))) x[m] = pen_x(x[m], rp.rp);
     }
     vis(g, q, wm, x);
   };
@@ -690,7 +813,7 @@ struct Keep {
 // and E >= E2), and only those reaching theta and the lane's 4th best get
 // their token noise.
 template <typename T>
-__device__ void race_row(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float theta,
+__device__ __noinline__ void race_row(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float theta,
                          const Keep& keep) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* em = P.emin + size_t(row) * size_t(P.G);
@@ -766,7 +889,7 @@ __device__ void race_row(const Params& P, RowSm& sm, const RowP& rp, int row, fl
       need &= need - 1u;
       const int id = member_id(bid, m);
       float xv = load_one<T>(P, row, id);
-      if (rp.pen && in_history(sm, rp, id)) xv = pen_x(xv, rp.rp);
+      if (rp.pen && in_history(sm.hash, rp, id)) xv = pen_x(xv, rp.rp);
       const float p = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xv, c1, c0)), Sf);
       if (!rbetter(__fdiv_rn(p, e2), id, top.r[kTC - 1], top.id[kTC - 1])) continue;
       const float E = __fadd_rn(e2, neglog(uniform_open(pick_word(philox_at(rp.key, uint32_t(id >> 2), kTagToken),
@@ -838,7 +961,7 @@ __device__ __forceinline__ unsigned long long efix(float x, float c1, float c0) 
 // (ids below it are known to be outside the kept set), the tie rank at the
 // boundary, then the race over the kept set.
 template <typename T>
-__device__ void exact_path(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, double S,
+__device__ __noinline__ void exact_path(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, double S,
                            float thr_m, float xf) {
   const int tid = threadIdx.x, lane = tid & 31;
   const int final_level = rp.pen ? 3 : P.dtype_level;
@@ -1108,7 +1231,7 @@ __device__ uint32_t kth_group_key(const Params& P, RowSm& sm, int row, int k) {
 // (reference rule), and the kept ones raced with exact noise.  Returns false
 // when a capacity ran out (the caller takes the exact path).
 template <typename T>
-__device__ bool small_k(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float thr_m) {
+__device__ __noinline__ bool small_k(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float thr_m) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = int(rp.k);
   const uint32_t tk = kth_group_key(P, sm, row, k);
@@ -1230,15 +1353,264 @@ __device__ bool small_k(const Params& P, RowSm& sm, const RowP& rp, int row, flo
   return true;
 }
 
-// ---------------------------------------------------------------- the row kernel
+// ---------------------------------------------------------------- 2. decide kernel
+struct alignas(16) DecSm {
+  RowP rp;
+  TaskRec tr[kMaxTasks];
+  int gl[kGList];                // groups expanded in the race round
+  int rs[kRescanCap];            // tasks whose every group is re-bounded
+  Cand wtop[kRowWarps][kTC];
+  Cand top[kTC];
+  int ngl, nrs, ntop;
+  uint32_t red_u[kRowWarps];
+  double red_d[kRowWarps][2];
+  long long red_l[kRowWarps][2];
+  int hash[kHashCap];            // last: allocated only for launches with a penalty history
+};
+
+__device__ __forceinline__ uint32_t dmax_u(uint32_t* red, uint32_t v) {
+  v = __reduce_max_sync(0xFFFFFFFFu, v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t r = 0u;
+#pragma unroll
+  for (int w = 0; w < kRowWarps; ++w) r = max(r, red[w]);
+  __syncthreads();
+  return r;
+}
+__device__ __forceinline__ uint32_t dmin_u(uint32_t* red, uint32_t v) {
+  v = __reduce_min_sync(0xFFFFFFFFu, v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t r = 0xFFFFFFFFu;
+#pragma unroll
+  for (int w = 0; w < kRowWarps; ++w) r = min(r, red[w]);
+  __syncthreads();
+  return r;
+}
+// Two doubles and two counts summed over the CTA (fixed order: deterministic).
+__device__ __forceinline__ void dsum2(DecSm& sm, double& a, double& b, long long& c, long long& d) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+    b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sm.red_d[w][0] = a; sm.red_d[w][1] = b;
+    sm.red_l[w][0] = c; sm.red_l[w][1] = d;
+  }
+  __syncthreads();
+  a = b = 0.0;
+  c = d = 0;
+#pragma unroll
+  for (int i = 0; i < kRowWarps; ++i) {
+    a += sm.red_d[i][0]; b += sm.red_d[i][1];
+    c += sm.red_l[i][0]; d += sm.red_l[i][1];
+  }
+  __syncthreads();
+}
+
+// Groups of scan task t: global ids [*g0, *g0 + *ng).
+__device__ __forceinline__ void task_groups(const Params& P, int t, int64_t* g0, int* ng) {
+  int s = 0;
+#pragma unroll 1
+  while (s + 1 < kNumSlices && P.tbase[s + 1] <= t) ++s;
+  const int tile0 = (t - P.tbase[s]) * P.tpw;
+  *g0 = P.gbase[s] + int64_t(tile0) * 32;
+  *ng = min(P.tpw, P.snt[s] - tile0) * 32;
+}
+
+// CTA-wide kTC best of every thread's Top4 (rho desc, id asc) into sm.top.
+__device__ __forceinline__ void merge_top(DecSm& sm, const Top4& top) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int h = 0;
+#pragma unroll
+  for (int i = 0; i < kTC; ++i) {
+    float r = -1.f, xx = 0.f, EE = 1.f;
+    int id = INT_MAX;
+#pragma unroll
+    for (int k = 0; k < kTC; ++k)
+      if (k == h) { r = top.r[k]; xx = top.x[k]; EE = top.E[k]; id = top.id[k]; }
+    const uint32_t kr = r >= 0.f ? __float_as_uint(r) + 1u : 0u;
+    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kr);
+    const uint32_t im = __reduce_min_sync(0xFFFFFFFFu, kr == km ? uint32_t(id) : 0xFFFFFFFFu);
+    const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kr == km && uint32_t(id) == im)) - 1;
+    const Cand c{__shfl_sync(0xFFFFFFFFu, r, src), __shfl_sync(0xFFFFFFFFu, xx, src),
+                 __shfl_sync(0xFFFFFFFFu, EE, src), int(im)};
+    if (lane == src && km != 0u) ++h;
+    if (lane == 0) sm.wtop[warp][i] = km != 0u ? c : Cand{-1.f, 0.f, 1.f, INT_MAX};
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // lane l holds candidate l of the 32 (8 warps x kTC)
+    Cand c = sm.wtop[lane / kTC][lane % kTC];
+    bool used = false;
+    int n = 0;
+#pragma unroll
+    for (int i = 0; i < kTC; ++i) {
+      const uint32_t kr = (!used && c.r >= 0.f) ? __float_as_uint(c.r) + 1u : 0u;
+      const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, kr);
+      const uint32_t im = __reduce_min_sync(0xFFFFFFFFu, kr == km ? uint32_t(c.id) : 0xFFFFFFFFu);
+      const int src = __ffs(__ballot_sync(0xFFFFFFFFu, kr == km && uint32_t(c.id) == im)) - 1;
+      const Cand w{__shfl_sync(0xFFFFFFFFu, c.r, src), __shfl_sync(0xFFFFFFFFu, c.x, src),
+                   __shfl_sync(0xFFFFFFFFu, c.E, src), int(im)};
+      if (lane == src) used = true;
+      if (lane == 0) sm.top[i] = km != 0u ? w : Cand{-1.f, 0.f, 1.f, INT_MAX};
+      n += km != 0u ? 1 : 0;
+    }
+    if (lane == 0) sm.ntop = n;
+  }
+  __syncthreads();
+}
+
+// One race round: every group whose noise bound can reach theta is expanded
+// exactly; sm.top gets the kTC best ratios, complete above theta.  Returns
+// false when a capacity ran out (the row then takes the exact path).
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads) row_kernel(const __grid_constant__ Params P) {
+__device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
+                           float theta) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ntask = P.tasks_row;
+  const bool cnoise = P.a.noise != nullptr;
+  // bound key threshold: 2^(bk - u) / S >= theta, with a margin for the
+  // approximate logs
+  const float lth = lg2_approx(theta) + u + lg2_approx(Sf) - 1e-3f;
+  if (tid == 0) { sm.ngl = 0; sm.nrs = 0; }
+  __syncthreads();
+  for (int i = tid; i < ntask; i += kRowThreads) {
+    const TaskRec& tr = sm.tr[i];
+    if (tr.bk0 >= lth && tr.bg0 != int(rp.s_gid)) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = tr.bg0;
+    if (tr.bk1 >= lth && tr.bg1 != int(rp.s_gid)) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = tr.bg1;
+    if (tr.bceil >= lth) {
+      const int at = atomicAdd(&sm.nrs, 1);
+      if (at < kRescanCap) sm.rs[at] = i;
+    }
+  }
+  if (tid == 0 && !cnoise && rp.s_gid >= 0) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = int(rp.s_gid);
+  __syncthreads();
+  const int nrs = sm.nrs;
+  if (nrs > kRescanCap) return false;
+  // tasks with three or more groups above the threshold: bound every group
+  for (int ri = warp; ri < nrs; ri += kRowWarps) {
+    const int t = sm.rs[ri];
+    const TaskRec& tr = sm.tr[t];
+    int64_t g0;
+    int ng;
+    task_groups(P, t, &g0, &ng);
+    for (int j = lane; j < ng; j += 32) {
+      const int64_t g = g0 + j;
+      if (g == tr.bg0 || g == tr.bg1 || g == rp.s_gid) continue;
+      const float gm = P.summ[size_t(row) * size_t(P.G) + size_t(g)].gmax;
+      if (!(gm > -INFINITY)) continue;
+      const float lo = cnoise ? P.emin[size_t(row) * size_t(P.G) + size_t(g)] : emin_lower(group_min_word(rp.key, g));
+      const float bk = lo > 0.f ? __fmul_rn(gm, rp.c1) - lg2_approx(lo) : INFINITY;
+      if (bk >= lth) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = int(g);
+    }
+  }
+  __syncthreads();
+  const int ngl = sm.ngl;
+  if (ngl >= kGList) return false;
+  // expansion: one group per thread
+  const float c1 = rp.c1;
+  const float pref = __fmul_rn(__fmul_rn(theta, Sf), 1.f - 1e-5f);   // e >= pref * E needed to reach theta
+  Top4 top;
+  top.init();
+  const unsigned char* rsrc = static_cast<const unsigned char*>(P.a.logits) + size_t(row) * size_t(P.a.ld) * P.esize;
+  const float* nz = cnoise ? P.a.noise + size_t(row) * size_t(P.a.noise_ld) : nullptr;
+  for (int i = tid; i < ngl; i += kRowThreads) {
+    const int64_t g = sm.gl[i];
+    const GrpGeo q = grp_geo(P, g);
+    float x[32];
+    load_members<T>(P, rsrc + size_t(q.base) * P.esize, q.lg >> 5, q.lg & 31, q.L, x);
+    const int bid = group_base_id(q);
+    if (rp.pen) {
+#pragma unroll
+      for (int m = 0; m < 32; ++m)
+        if (m < q.n && in_history(sm.hash, rp, member_id(bid, m))) x[m] = pen_x(x[m], rp.rp);
+    }
+    const int n = q.n;
+    if (cnoise) {
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        if (m >= n) continue;
+        const float e = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
+        const int id = member_id(bid, m);
+        const float E = __ldg(nz + id);
+        if (!(e >= __fmul_rn(pref, E))) continue;
+        top.add(__fdiv_rn(__fdiv_rn(e, Sf), E), x[m], E, id);
+      }
+      continue;
+    }
+    const bool holds = g == rp.s_gid;
+    const U4 wd = philox_at(rp.key, uint32_t(g), kTagGroup);
+    int am;
+    float emin;
+    if (holds) {
+      am = rp.s_mem;
+      emin = rp.e_root;
+    } else {
+      am = int(select_index32(wd.y, uint32_t(n)));
+      const float l = neglog(uniform_open(group_min_word(rp.key, g)));
+      emin = __fadd_rn(rp.e_root, n == 32 ? __fmul_rn(l, 0.03125f) : __fdiv_rn(l, float(n)));
+    }
+    int a2 = -1;
+    float e2 = INFINITY;
+    if (n >= 2) {
+      e2 = __fadd_rn(emin, __fdiv_rn(neglog(uniform_open(wd.z)), float(n - 1)));
+      const int i2 = int(select_index32(wd.w, uint32_t(n - 1)));
+      a2 = i2 < am ? i2 : i2 + 1;
+    }
+    const float pre2 = __fmul_rn(pref, e2);
+    uint32_t need = 0u;
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      if (m >= n) continue;
+      const float e = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
+      const int id = member_id(bid, m);
+      if (m == am) {
+        if (e >= __fmul_rn(pref, emin)) top.add(__fdiv_rn(__fdiv_rn(e, Sf), emin), x[m], emin, id);
+      } else if (m == a2) {
+        if (e >= pre2) top.add(__fdiv_rn(__fdiv_rn(e, Sf), e2), x[m], e2, id);
+      } else if (e >= pre2) {
+        need |= 1u << m;
+      }
+    }
+#pragma unroll 1
+    while (need) {
+      const int m = __ffs(need) - 1;
+      need &= need - 1u;
+      const int id = member_id(bid, m);
+      float xv = load_one<T>(P, row, id);
+      if (rp.pen && in_history(sm.hash, rp, id)) xv = pen_x(xv, rp.rp);
+      const float p = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xv, c1, c0)), Sf);
+      if (!rbetter(__fdiv_rn(p, e2), id, top.r[kTC - 1], top.id[kTC - 1])) continue;
+      const float E = __fadd_rn(e2, neglog(uniform_open(pick_word(philox_at(rp.key, uint32_t(id >> 2), kTagToken),
+                                                                   uint32_t(id & 3)))));
+      top.add(__fdiv_rn(p, E), xv, E, id);
+    }
+  }
+  merge_top(sm, top);
+  return true;
+}
+
+__device__ __forceinline__ void push_fin(const Params& P, int row, unsigned kind) {
+  const unsigned at = atomicAdd(&P.ctl->n_fin, 1u);
+  P.flist[at] = int(unsigned(row) | (kind << 28));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  RowSm& sm = *reinterpret_cast<RowSm*>(smem_raw);
+  DecSm& sm = *reinterpret_cast<DecSm*>(smem_raw);
   const int tid = threadIdx.x;
   const int row = blockIdx.x;
   const int64_t V = P.a.vocab;
-  if (row == 0 && tid == 0) P.ctl->err = 0u;
+  const int ntask = P.tasks_row;
+  const TaskRec* trg = P.trec + size_t(row) * size_t(ntask);
+  for (int i = tid; i < ntask; i += kRowThreads) sm.tr[i] = trg[i];
   if (tid == 0) {
     RowP r = row_params(P, row);
     if (!P.a.noise && r.kind != kKindGreedy && r.kind != kKindArgmax) {
@@ -1254,49 +1626,24 @@ __global__ void __launch_bounds__(kRowThreads) row_kernel(const __grid_constant_
   }
   __syncthreads();
   const RowP rp = sm.rp;
-  const GroupSum* gs = P.summ + size_t(row) * size_t(P.G);
   const bool idx_mode = rp.kind == kKindGreedy || rp.kind == kKindArgmax;
-  // one pass: row max (NaN-aware) and, in each thread's own running scale,
-  // the sum of the group terms
   uint32_t kmax = 0u;
-  float mt = -INFINITY;
-  double st = 0.0;
-  const int64_t nq = (P.G + 3) / 4;
-#pragma unroll 2
-  for (int64_t qd = tid; qd < nq; qd += kRowThreads) {
-    GroupSum sg[4];
-    if (qd * 4 + 4 <= P.G) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(gs + qd * 4));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(gs + qd * 4 + 2));
-      sg[0] = GroupSum{a.x, a.y};
-      sg[1] = GroupSum{a.z, a.w};
-      sg[2] = GroupSum{b.x, b.y};
-      sg[3] = GroupSum{b.z, b.w};
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sg[j] = qd * 4 + j < P.G ? gs[qd * 4 + j] : GroupSum{-INFINITY, 0.f};
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      kmax = max(kmax, nan_key(sg[j].gmax));
-      if (!idx_mode && sg[j].gmax > -INFINITY) {
-        const float ug = __fmul_rn(sg[j].gmax, rp.c1);
-        if (ug > mt) {
-          st = st * double(qe_ex2_ftz(__fsub_rn(mt, ug))) + double(sg[j].aux);
-          mt = ug;
-        } else {
-          st += double(sg[j].aux * qe_ex2_ftz(__fsub_rn(ug, mt)));
-        }
-      }
-    }
-  }
-  kmax = block_max_u(sm, kmax);
+  for (int i = tid; i < ntask; i += kRowThreads) kmax = max(kmax, nan_key(sm.tr[i].tmax));
+  kmax = dmax_u(sm.red_u, kmax);
   const float xmax = kmax == 0xFFFFFFFFu ? __int_as_float(0x7FFFFFFF) : key_to_float(kmax);
   const float u = __fmul_rn(xmax, rp.c1);
   bool fin = finite_f(xmax) && finite_f(u);
   double S = 0.0;
   if (!idx_mode && fin) {
-    S = block_sum_d(sm, mt > -INFINITY && finite_f(mt) ? st * double(qe_ex2_ftz(__fsub_rn(mt, u))) : 0.0);
+    double a = 0.0, b = 0.0;
+    long long c = 0, d = 0;
+    for (int i = tid; i < ntask; i += kRowThreads) {
+      const TaskRec& tr = sm.tr[i];
+      const float ut = __fmul_rn(tr.tmax, rp.c1);
+      if (tr.tmax > -INFINITY && finite_f(ut)) a += tr.tsum * double(qe_ex2_ftz(__fsub_rn(ut, u)));
+    }
+    dsum2(sm, a, b, c, d);
+    S = a;
     if (!(S > 0.0) || !(float(S) < INFINITY)) fin = false;
   }
   if (tid == 0 && P.a.out_norm)
@@ -1307,13 +1654,21 @@ __global__ void __launch_bounds__(kRowThreads) row_kernel(const __grid_constant_
     uint32_t first = 0xFFFFFFFFu;
     if (xmax > -INFINITY || xmax != xmax) {
       const bool xn = xmax != xmax;
-      for (int64_t g = tid; g < P.G; g += kRowThreads) {
-        const GroupSum sg = gs[g];
-        if (!(xn ? sg.gmax != sg.gmax : sg.gmax == xmax)) continue;
-        const GrpGeo q = grp_geo(P, g);
-        first = min(first, uint32_t(q.base + member_offset(q.lg, __float_as_int(sg.aux))));
+      const int lane = tid & 31, warp = tid >> 5;
+      for (int t = warp; t < ntask; t += kRowWarps) {
+        const float tm = sm.tr[t].tmax;
+        if (!(xn ? tm != tm : tm == xmax)) continue;
+        int64_t g0;
+        int ng;
+        task_groups(P, t, &g0, &ng);
+        for (int j = lane; j < ng; j += 32) {
+          const GroupSum sg = P.summ[size_t(row) * size_t(P.G) + size_t(g0 + j)];
+          if (!(xn ? sg.gmax != sg.gmax : sg.gmax == xmax)) continue;
+          const GrpGeo q = grp_geo(P, g0 + j);
+          first = min(first, uint32_t(q.base + member_offset(q.lg, __float_as_int(sg.aux))));
+        }
       }
-      first = block_min_u(sm, first);
+      first = dmin_u(sm.red_u, first);
     } else {
       first = 0u;   // every logit is -inf: torch.argmax returns 0
     }
@@ -1321,94 +1676,288 @@ __global__ void __launch_bounds__(kRowThreads) row_kernel(const __grid_constant_
     write_row(P, row, first, status, rp.kind == kKindArgmax && fin ? 1 : 0);
     return;
   }
-  if (rp.pen) hash_build(sm, rp, V);
   const float c0 = -u;
   const float Sf = float(S);
   const float thr_m = rp.m_on ? __fmul_rn(rp.minp, __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xmax, rp.c1, c0)), Sf)) : 0.f;
-  if (rp.kind == kKindSmallK) {
-    if (small_k<T>(P, sm, rp, row, c0, Sf, thr_m)) return;
-    exact_path<T>(P, sm, rp, row, c0, Sf, S, thr_m, -INFINITY);
+  RowState* rs = P.rstate + row;
+  if (tid == 0) {
+    rs->xmax = xmax; rs->u = u; rs->Sf = Sf; rs->thr_m = thr_m; rs->S = S;
+    rs->ncand = 0; rs->done = 0u;
+  }
+  if (rp.kind == kKindSmallK || rp.exact) {
+    if (tid == 0) push_fin(P, row, rp.kind == kKindSmallK ? kFinSmallK : kFinExact);
     return;
   }
-  if (rp.exact) {
-    exact_path<T>(P, sm, rp, row, c0, Sf, S, thr_m, -INFINITY);
-    return;
-  }
-  const Keep all{0, 0, 0u, 1, INT_MAX};
-  // first race: complete above 1/4 (the best ratio of a race is below that
-  // with probability e^-4); enough when its best is in the kept set
+  if (rp.pen) hash_build(sm.hash, rp, V);
+  // race: complete above 1/4 (the best ratio of a race is below that with
+  // probability e^-4), then above 1/64
   float theta = 0.25f;
-  race_row<T>(P, sm, rp, row, c0, Sf, theta, all);
-  if (!rp.filtered) {
-    if (!(sm.ntop > 0 && sm.top[0].r >= theta)) race_row<T>(P, sm, rp, row, c0, Sf, 0.f, all);
-    if (sm.ntop == 0 && tid == 0) atomicOr(&P.ctl->err, 4u);
-    write_row(P, row, sm.ntop > 0 ? sm.top[0].id : -1, 0, V);
+  bool ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta);
+  if (ok && !(sm.ntop > 0 && sm.top[0].r >= theta)) {
+    theta = 1.f / 64.f;
+    ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta);
+  }
+  if (!ok || !(sm.ntop > 0 && sm.top[0].r >= theta)) {
+    if (tid == 0) push_fin(P, row, kFinExact);
     return;
   }
-  // kept-set test of the complete candidates, in race order; a second race
-  // (complete above 1/64) when the first did not settle the row
+  if (!rp.filtered) {
+    write_row(P, row, sm.top[0].id, 0, V);
+    return;
+  }
+  // kept-set test of the candidates in race order: bounds from the task
+  // records, then from the group records of the tasks that can hold ids
+  // ahead; what they cannot settle is counted exactly by the count kernel
+  const int ntop = sm.ntop;
+  const double tpS = double(rp.tp) * S;
 #pragma unroll 1
-  for (int pass = 0; pass < 2; ++pass) {
-    if (pass == 1) {
-      theta = 1.f / 64.f;
-      race_row<T>(P, sm, rp, row, c0, Sf, theta, all);
+  for (int i = 0; i < ntop; ++i) {
+    const Cand c = sm.top[i];
+    if (!(c.r >= theta)) break;
+    const float e = qe_ex2_ftz(__fmaf_rn(c.x, rp.c1, c0));
+    if (rp.m_on && __fdiv_rn(e, Sf) < thr_m) continue;   // removed by min-p
+    double U = 0.0, Lm = 0.0;
+    long long N = 0, Lc = 0;
+    for (int t = tid; t < ntask; t += kRowThreads) {
+      const TaskRec& tr = sm.tr[t];
+      if (!(tr.tmax >= c.x)) continue;
+      U += tr.tsum * double(qe_ex2_ftz(__fsub_rn(__fmul_rn(tr.tmax, rp.c1), u)));
+      int64_t g0;
+      int ng;
+      task_groups(P, t, &g0, &ng);
+      N += (long long)ng * 32;
     }
-    const int ntop = sm.ntop;
-#pragma unroll 1
-    for (int i = 0; i < kTC; ++i) {
-      if (i >= ntop) break;
-      const Cand c = sm.top[i];
-      if (!(c.r >= theta)) break;
-      const float e = qe_ex2_ftz(__fmaf_rn(c.x, rp.c1, c0));
-      if (rp.m_on && __fdiv_rn(e, Sf) < thr_m) continue;
-      // bound from the summaries: every id ahead lies in a group whose max
-      // is at or above the candidate
-      double ub = 0.0;
-      long long nb = 0;
-      for (int64_t g = tid; g < P.G; g += kRowThreads) {
-        const GroupSum sg = gs[g];
-        if (!(sg.gmax >= c.x)) continue;
-        ub += double(sg.aux * qe_ex2_ftz(__fsub_rn(__fmul_rn(sg.gmax, rp.c1), u)));
-        nb += 32;
-      }
-      ub = block_sum_d(sm, ub);
-      nb = block_sum_l(sm, nb);
-      bool in_k = (!rp.k_on || nb - 1 < rp.k) && (!rp.p_on || ub * (1.0 + 1e-5) - double(e) <= double(rp.tp) * S);
-      if (!in_k) {
-        // exact count and mass ahead over those groups
-        double ms = 0.0;
-        long long ct = 0;
-        auto want = [&](int64_t, const GroupSum& sg, uint32_t) -> bool { return sg.gmax >= c.x; };
-        auto vis = [&](int64_t, const GrpGeo& q, uint32_t, const float (&x)[32]) {
-          const int bid = group_base_id(q);
-          float part = 0.f;
-#pragma unroll
-          for (int m = 0; m < 32; ++m) {
-            const float v = x[m];
-            if (m < q.n && (v > c.x || (v == c.x && member_id(bid, m) < c.id))) {
-              part += qe_ex2_ftz(__fmaf_rn(v, rp.c1, c0));
-              ct += 1;
-            }
+    dsum2(sm, U, Lm, N, Lc);
+    bool in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
+    bool in_k = !rp.k_on || N - 1 < rp.k;
+    bool out = false;
+    if (!(in_p && in_k)) {
+      // group level over the tasks whose max is at or above the candidate
+      U = 0.0; N = 0;
+      const int lane = tid & 31, warp = tid >> 5;
+      for (int t = warp; t < ntask; t += kRowWarps) {
+        if (!(sm.tr[t].tmax >= c.x)) continue;
+        int64_t g0;
+        int ng;
+        task_groups(P, t, &g0, &ng);
+        const GroupSum* gs = P.summ + size_t(row) * size_t(P.G) + size_t(g0);
+        for (int j = lane; j < ng; j += 32) {
+          const GroupSum sg = gs[j];
+          if (!(sg.gmax >= c.x)) continue;
+          const float ug = __fmul_rn(sg.gmax, rp.c1);
+          U += double(sg.aux) * double(qe_ex2_ftz(__fsub_rn(ug, u)));
+          N += 32;
+          if (sg.gmax > c.x) {
+            Lm += double(qe_ex2_ftz(__fmaf_rn(sg.gmax, rp.c1, c0)));
+            Lc += 1;
           }
-          ms += double(part);
-        };
-        lane_visit<T, false>(P, sm, rp, row, want, vis);
-        ms = block_sum_d(sm, ms);
-        ct = block_sum_l(sm, ct);
-        in_k = (!rp.k_on || ct < rp.k) && (!rp.p_on || ms <= double(rp.tp) * S);
-        if (!in_k) {
-          // every id after it in the order is outside as well: a floor
-          if (pass == 1 || i + 1 < ntop) continue;
         }
       }
-      if (in_k) {
-        write_row(P, row, c.id, 0, 0);
-        return;
+      dsum2(sm, U, Lm, N, Lc);
+      in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
+      in_k = !rp.k_on || N - 1 < rp.k;
+      out = (rp.p_on && Lm > tpS * (1.0 + 1e-6)) || (rp.k_on && Lc >= rp.k);
+    }
+    if (in_p && in_k) {
+      write_row(P, row, c.id, 0, 0);
+      return;
+    }
+    if (out) continue;
+    // undecided: the count kernel counts this and every later candidate
+    if (tid == 0) {
+      int n = 0;
+      for (int j = i; j < ntop; ++j) {
+        const Cand cj = sm.top[j];
+        if (!(cj.r >= theta)) break;
+        rs->cand[n] = cj;
+        rs->cmass[n] = 0ull;
+        rs->ccnt[n] = 0ull;
+        ++n;
+      }
+      rs->ncand = n;
+      const unsigned at = atomicAdd(&P.ctl->n_pend, 1u);
+      P.plist[at] = row;
+    }
+    return;
+  }
+  if (tid == 0) push_fin(P, row, kFinExact);   // every candidate is outside the kept set
+}
+
+// ---------------------------------------------------------------- 3. count kernel
+// Exact count and mass of the ids ahead of each pending candidate, one warp
+// per (pending row, scan task); the warp that completes a row decides it.
+template <typename T>
+__global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constant__ Params P) {
+  __shared__ uint32_t pen_bits[kSumThreads / 32][64];
+  const unsigned npend = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_pend);
+  if (npend == 0u) return;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const long long items = (long long)npend * P.tasks_row;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  const KernelArgs& a = P.a;
+#pragma unroll 1
+  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + wib; item < items; item += nw) {
+    const int row = P.plist[item / P.tasks_row];
+    const int t = int(item % P.tasks_row);
+    RowState* rs = P.rstate + row;
+    const int nc = rs->ncand;
+    Cand cand[kTC];
+    float xlo = INFINITY;
+#pragma unroll
+    for (int i = 0; i < kTC; ++i) {
+      cand[i] = i < nc ? rs->cand[i] : Cand{-1.f, INFINITY, 1.f, -1};
+      if (i < nc) xlo = fminf(xlo, cand[i].x);
+    }
+    const float c1 = temp_coef(a.temperatures[row]);
+    const float c0 = -rs->u;
+    float rpen = 1.f;
+    int hl = 0;
+    if (a.history && a.rep_penalties) {
+      rpen = a.rep_penalties[row];
+      hl = a.history_lens ? a.history_lens[row] : int(a.history_ld);
+      hl = hl < 0 ? 0 : (hl > int(a.history_ld) ? int(a.history_ld) : hl);
+    }
+    const bool pen = hl > 0 && !(rpen == 1.f);
+    const int32_t* hist = pen ? a.history + row * a.history_ld : nullptr;
+    int s = 0;
+#pragma unroll 1
+    while (s + 1 < kNumSlices && P.tbase[s + 1] <= t) ++s;
+    const int tile0 = (t - P.tbase[s]) * P.tpw;
+    const int ntile = min(P.tpw, P.snt[s] - tile0);
+    const int64_t sa = P.sstart[s];
+    const int L = int(P.sstart[s + 1] - sa);
+    const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
+    const GroupSum* gs = P.summ + size_t(row) * size_t(P.G) + size_t(P.gbase[s] + int64_t(tile0) * 32);
+    unsigned long long ms[kTC] = {0ull, 0ull, 0ull, 0ull}, ct[kTC] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll 1
+    for (int tp = 0; tp < ntile; tp += 2) {
+      const int nt = min(2, ntile - tp);
+      if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tile0 + tp, nt, L);
+#pragma unroll 1
+      for (int tt = 0; tt < nt; ++tt) {
+        const int tile = tile0 + tp + tt;
+        const GroupSum sg = gs[(tp + tt) * 32 + lane];
+        if (!(sg.gmax >= xlo)) continue;
+        float x[32];
+        load_members<T>(P, src, tile, lane, L, x);
+        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
+        if (pb) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m)
+            if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
+        }
+        const int bid = int(sa) + tile * kTile + lane * 8;
+#pragma unroll
+        for (int m = 0; m < 32; ++m) {
+          const float v = x[m];
+          if (!(v >= xlo)) continue;
+          const int id = member_id(bid, m);
+          const unsigned long long f = efix(v, c1, c0);
+#pragma unroll
+          for (int i = 0; i < kTC; ++i) {
+            if (v > cand[i].x || (v == cand[i].x && id < cand[i].id)) {
+              ms[i] += f;
+              ct[i] += 1ull;
+            }
+          }
+        }
       }
     }
+#pragma unroll
+    for (int i = 0; i < kTC; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ms[i] += __shfl_xor_sync(0xFFFFFFFFu, ms[i], o);
+        ct[i] += __shfl_xor_sync(0xFFFFFFFFu, ct[i], o);
+      }
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kTC; ++i) {
+        if (i < nc && ms[i]) atomicAdd(&rs->cmass[i], ms[i]);
+        if (i < nc && ct[i]) atomicAdd(&rs->ccnt[i], ct[i]);
+      }
+      __threadfence();
+      const unsigned d = atomicAdd(&rs->done, 1u);
+      if (d == unsigned(P.tasks_row - 1)) {
+        __threadfence();
+        // the row's counts are complete: first candidate inside the kept set
+        const float tp_ = a.top_ps ? a.top_ps[row] : 1.f;
+        const bool p_on = (a.flags & QE_FLAG_USE_TOP_P) && a.top_ps && tp_ < 1.f;
+        const long long kraw = a.top_ks ? (long long)a.top_ks[row] : 0;
+        const bool k_on = kraw > 0 && kraw < a.vocab;
+        const double S = rs->S;
+        const unsigned long long tfix =
+            p_on ? static_cast<unsigned long long>(floor(double(tp_) * S * 1099511627776.0)) : ~0ull;
+        const float Sf = rs->Sf, thr_m = rs->thr_m;
+        const bool m_on = a.min_ps && a.min_ps[row] > 0.f;
+        long long win = -1;
+        for (int i = 0; i < nc; ++i) {
+          const unsigned long long mm = atomicAdd(&rs->cmass[i], 0ull);
+          const unsigned long long cc = atomicAdd(&rs->ccnt[i], 0ull);
+          if (m_on && __fdiv_rn(qe_ex2_ftz(__fmaf_rn(cand[i].x, c1, c0)), Sf) < thr_m) continue;
+          if ((!k_on || (long long)cc < kraw) && mm <= tfix) {
+            win = cand[i].id;
+            break;
+          }
+        }
+        if (win >= 0) {
+          a.out_ids[row] = win;
+          if (a.out_status) a.out_status[row] = 0;
+          if (a.out_kept) a.out_kept[row] = 0;
+        } else {
+          push_fin(P, row, kFinExact);
+        }
+      }
+    }
+    __syncwarp();
   }
-  exact_path<T>(P, sm, rp, row, c0, Sf, S, thr_m, -INFINITY);
 }
+
+// ---------------------------------------------------------------- 4. finish kernel
+// Rows that need the kept set itself: small top-k rows, rows whose race
+// candidates all fall outside the kept set, rows whose kept-set size was
+// asked for.  Persistent CTAs over the finish list.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) finish_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  RowSm& sm = *reinterpret_cast<RowSm*>(smem_raw);
+  const unsigned nfin = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_fin);
+  const int tid = threadIdx.x;
+  const int64_t V = P.a.vocab;
+#pragma unroll 1
+  for (unsigned li = blockIdx.x; li < nfin; li += gridDim.x) {
+    const unsigned ent = unsigned(P.flist[li]);
+    const int row = int(ent & 0x0FFFFFFFu);
+    const unsigned kind = ent >> 28;
+    if (tid == 0) {
+      RowP r = row_params(P, row);
+      if (!P.a.noise) {
+        const NoiseRoot rt = noise_root(r.key, V);
+        int64_t gsd = -1;
+        int rm = 0;
+        token_group_p(P, rt.s, &gsd, &rm);
+        r.e_root = rt.e_root;
+        r.s_gid = gsd;
+        r.s_mem = rm;
+      }
+      sm.rp = r;
+    }
+    __syncthreads();
+    const RowP rp = sm.rp;
+    const RowState* rs = P.rstate + row;
+    const float u = rs->u, Sf = rs->Sf, thr_m = rs->thr_m;
+    const double S = rs->S;
+    if (rp.pen) hash_build(sm.hash, rp, V);
+    if (kind == kFinSmallK) {
+      if (!small_k<T>(P, sm, rp, row, -u, Sf, thr_m)) exact_path<T>(P, sm, rp, row, -u, Sf, S, thr_m, -INFINITY);
+    } else {
+      exact_path<T>(P, sm, rp, row, -u, Sf, S, thr_m, -INFINITY);
+    }
+    __syncthreads();
+  }
+}
+
 
 // ---------------------------------------------------------------- host
 struct DevInfo {
@@ -1418,9 +1967,15 @@ struct DevInfo {
 std::mutex g_mu;
 DevInfo g_dev[64];
 
+constexpr size_t kDecSmFull = sizeof(DecSm);
+constexpr size_t kDecSmNoHash = offsetof(DecSm, hash);
+
 template <typename T>
 cudaError_t prepare() {
-  return cudaFuncSetAttribute(row_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(RowSm)));
+  cudaError_t e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(RowSm)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decide_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmFull));
+  return e;
 }
 
 // Kernel attributes, set once per device (they are per-device state).
@@ -1443,11 +1998,23 @@ int device_setup(int* sms) {
   return QE_OK;
 }
 
+template <typename T>
+void launch_all(const Params& P, unsigned g1, int wpc, unsigned g2, size_t dec_smem, unsigned g3, unsigned g4,
+                cudaStream_t stream) {
+  scan_kernel<T><<<g1, wpc * 32, 0, stream>>>(P);
+  decide_kernel<T><<<g2, kRowThreads, dec_smem, stream>>>(P);
+  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P);
+  finish_kernel<T><<<g4, kRowThreads, sizeof(RowSm), stream>>>(P);
+}
+
 }  // namespace st
 
 bool stream_supports(int64_t vocab) { return vocab >= 1 && vocab < (int64_t(1) << 24); }
 
-size_t stream_workspace_bytes(int64_t batch, int64_t vocab) { return st::make_layout(batch, vocab).total; }
+size_t stream_workspace_bytes(int64_t batch, int64_t vocab) {
+  const size_t a = st::make_layout(batch, vocab, 2).total, b = st::make_layout(batch, vocab, 4).total;
+  return a > b ? a : b;
+}
 
 const void* stream_error_word(const void* workspace) {
   return static_cast<const char*>(workspace) + offsetof(st::Ctl, err);
@@ -1456,8 +2023,8 @@ const void* stream_error_word(const void* workspace) {
 int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   using namespace st;
   const int esize = ka.dtype == QE_DTYPE_F32 ? 4 : 2;
-  const Layout L = make_layout(ka.batch, ka.vocab);
-  if (ka.batch >= (int64_t(1) << 31)) return set_error(QE_ERR_UNSUPPORTED, "batch too large");
+  if (ka.batch >= (int64_t(1) << 28)) return set_error(QE_ERR_UNSUPPORTED, "batch too large");
+  const Layout L = make_layout(ka.batch, ka.vocab, esize);
   int sms = 0;
   const int rc = device_setup(&sms);
   if (rc != QE_OK) return rc;
@@ -1469,7 +2036,7 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   P.vec_ok = (lp % 16 == 0) && ((ka.ld * esize) % 16 == 0);
   const uintptr_t np = reinterpret_cast<uintptr_t>(ka.noise);
   P.noise_vec = ka.noise && (np % 16 == 0) && ((ka.noise_ld * 4) % 16 == 0);
-  P.tpw = esize == 4 ? 1 : 2;
+  P.tpw = L.tpw;
   P.force_exact = ka.out_kept != nullptr;
   P.dtype_level = ka.dtype == QE_DTYPE_BF16 ? 1 : ka.dtype == QE_DTYPE_F16 ? 2 : 3;
   P.G = L.G;
@@ -1488,30 +2055,31 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   P.gbase[kNumSlices] = gb;
   P.tbase[kNumSlices] = tb;
   P.tasks_row = tb;
+  if (tb != L.tasks || gb != L.G) return set_error(QE_ERR_CUDA, "stream sampler: inconsistent layout");
   char* base = static_cast<char*>(ka.workspace);
   P.ctl = reinterpret_cast<Ctl*>(base);
   P.summ = reinterpret_cast<GroupSum*>(base + L.summ);
+  P.trec = reinterpret_cast<TaskRec*>(base + L.trec);
   P.emin = reinterpret_cast<float*>(base + L.emin);
-  // summary kernel: one warp per task; narrower CTAs when there are few
-  // tasks, so that they spread over the SMs
+  P.rstate = reinterpret_cast<RowState*>(base + L.rstate);
+  P.plist = reinterpret_cast<int*>(base + L.plist);
+  P.flist = reinterpret_cast<int*>(base + L.flist);
+  // scan: one warp per task; narrower CTAs when there are few tasks, so that
+  // they spread over the SMs
   const long long tasks = (long long)ka.batch * tb;
   int wpc = kSumThreads / 32;
   while (wpc > 1 && tasks < (long long)wpc * sms * 2) wpc >>= 1;
   const unsigned g1 = unsigned((tasks + wpc - 1) / wpc);
   const unsigned g2 = unsigned(ka.batch);
+  const bool pen = ka.history && ka.rep_penalties;
+  const size_t dec_smem = pen ? kDecSmFull : kDecSmNoHash;
+  const long long cwarps = (tasks + 7) / 8;
+  const unsigned g3 = unsigned(cwarps < (long long)sms * 4 ? (cwarps < 1 ? 1 : cwarps) : (long long)sms * 4);
+  const unsigned g4 = unsigned(ka.batch < (int64_t)sms * 2 ? ka.batch : (int64_t)sms * 2);
   switch (ka.dtype) {
-    case QE_DTYPE_F32:
-      summ_kernel<float><<<g1, wpc * 32, 0, stream>>>(P);
-      row_kernel<float><<<g2, kRowThreads, sizeof(RowSm), stream>>>(P);
-      break;
-    case QE_DTYPE_BF16:
-      summ_kernel<__nv_bfloat16><<<g1, wpc * 32, 0, stream>>>(P);
-      row_kernel<__nv_bfloat16><<<g2, kRowThreads, sizeof(RowSm), stream>>>(P);
-      break;
-    default:
-      summ_kernel<__half><<<g1, wpc * 32, 0, stream>>>(P);
-      row_kernel<__half><<<g2, kRowThreads, sizeof(RowSm), stream>>>(P);
-      break;
+    case QE_DTYPE_F32: launch_all<float>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
+    case QE_DTYPE_BF16: launch_all<__nv_bfloat16>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
+    default: launch_all<__half>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("stream sampler launch: ") + cudaGetErrorString(e));

@@ -15,7 +15,7 @@ def device_logits(w: W.Workload, dev="cuda") -> torch.Tensor:
 
 
 def run(sampler, w: W.Workload, noise=None, *, seed=None, step=None, top_k=True,
-        all_greedy=None, out_probs=None, out_status=None, logits=None):
+        all_greedy=None, out_probs=None, out_status=None, logits=None, **extra):
     dev = "cuda"
     lg = device_logits(w, dev) if logits is None else logits
     kw = {}
@@ -31,6 +31,6 @@ def run(sampler, w: W.Workload, noise=None, *, seed=None, step=None, top_k=True,
         all_greedy = bool(np.all(w.temperatures <= 1e-5))
     ids = sampler(lg, torch.from_numpy(w.temperatures).to(dev), torch.from_numpy(w.top_ps).to(dev),
                   all_greedy=all_greedy, use_top_p=w.use_top_p, seed=seed, step=step,
-                  out_probs=out_probs, out_status=out_status, **kw)
+                  out_probs=out_probs, out_status=out_status, **kw, **extra)
     torch.cuda.synchronize()
     return ids.cpu().numpy()
