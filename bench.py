@@ -95,41 +95,41 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def cpu_baseline(cfg: int, rows: int, seed_rows: int = 0):
-    """Time the oracle (CPU restatement of the reference sampler) on a bounded
-    sample of the workload with a spawn pool over all host cores."""
-    import multiprocessing as mp
-    from oracle import cpu_bench
-    cores = os.cpu_count() or 1
-    ctx = mp.get_context("spawn")
-    n = max(rows, cores)
-    with ctx.Pool(cores) as pool:
-        pool.map(cpu_bench.warm, range(cores))
-        t0 = time.perf_counter()
-        done = sum(pool.map(cpu_bench.sample_rows, [(cfg, i) for i in range(n)]))
-        dt = time.perf_counter() - t0
-    return {"value": done / dt, "unit": "rows/s", "cores": cores, "kind": "port",
-            "sample": f"{done} rows of config {cfg} (V=248,320) through oracle/sampler_oracle.py, "
-                      f"one row per task on a {cores}-process spawn pool"}
+def cpu_baseline(cfg: int, rows: int | None = None):
+    """Time the oracle (CPU restatement of the reference sampler) on the host
+    cores over a bounded sample of the workload: the first `rows` rows of
+    configuration `cfg` (all B by default), one row per task on a spawn pool
+    that holds the pre-generated workload in shared memory."""
+    from oracle.cpu_bench import CpuSampler
+    with CpuSampler(cfg) as cs:
+        n = cs.B if rows is None else min(rows, cs.B)
+        dt = cs.step(n)
+        return {"value": n / dt, "unit": "rows/s", "cores": cs.procs, "kind": "port",
+                "sample": f"{n} rows of {cs.name} (V={cs.V:,}) through oracle/sampler_oracle.py "
+                          f"(numpy restatement of the reference sampler) on a {cs.procs}-process pool; "
+                          f"workload generated before timing"}
 
 
 def run_reference(args, rank: int, world: int):
+    """The reference algorithm's CPU implementation (the oracle port) on the
+    host cores, full config batches per step, rank 0 only."""
     if rank != 0:
         return
-    per_step_rows = max(8, os.cpu_count() or 1)
-    vals = []
-    base = None
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args.config, per_step_rows)
-        if i >= args.warmup:
-            vals.append(r["value"])
-        base = r
-    v = statistics.median(vals)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * 256 / v,
+    from oracle.cpu_bench import CpuSampler
+    with CpuSampler(args.config) as cs:
+        for _ in range(args.warmup):
+            cs.step()
+        times = [cs.step() for _ in range(args.steps)]
+    total = sum(times)
+    v = cs.B * args.steps / total
+    line = {"impl": "reference", "metric": METRIC if args.config == 3 else f"sampled rows/sec, config {args.config}",
+            "value": v, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": f"config{args.config}", "B": 256, "V": 248320},
-            "cpu_baseline": dict(base, value=v),
+            "data": "synthetic", "config": {"workload": cs.name, "B": cs.B, "V": cs.V},
+            "cpu_baseline": {"value": v, "unit": "rows/s", "cores": cs.procs, "kind": "port",
+                             "sample": f"every step samples all {cs.B} rows of {cs.name} through "
+                                       f"oracle/sampler_oracle.py on a {cs.procs}-process pool"},
             "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -229,16 +229,88 @@ def run_vocab_sharded(args, rank: int, world: int, local: int):
         dist.destroy_process_group()
 
 
+LAUNCHES_PER_CALL = 6   # scan, decide, count, retry, count, finish (qe_sample_stream.cu)
+
+
+def prepare_config(cfg: int, dev, mode: str = "philox"):
+    """Device inputs of a configuration: rotating logits buffers (together
+    more than 2x L2, so that L2 never serves the logits between steps) and
+    the per-row parameters."""
+    import torch
+    from qedge_b200 import workloads as W
+    w = W.CONFIGS[cfg]()
+    esize = 4 if w.dtype == "f32" else 2
+    bytes_per_batch = w.B * w.V * esize
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / bytes_per_batch)) + 1)
+    base = W.to_device(w, dev)
+    bufs = [base] + [base.roll(shifts=i * 997, dims=1).contiguous() for i in range(1, nbuf)]
+    kw = {"top_ks": torch.from_numpy(w.top_ks.astype(np.int32)).to(dev)}
+    hist_bytes = 0
+    if w.history is not None:
+        kw.update(rep_penalties=torch.from_numpy(w.rep_penalties).to(dev),
+                  history=torch.from_numpy(w.history).to(dev),
+                  history_lens=torch.from_numpy(w.history_lens).to(dev))
+        hist_bytes = int(w.history_lens.sum()) * 4
+    if mode == "noise":
+        kw["noise"] = torch.from_numpy(W.exp_noise(w.B, w.V, 1)).to(dev)
+    temps = torch.from_numpy(w.temperatures).to(dev)
+    tps = torch.from_numpy(w.top_ps).to(dev)
+    alg = bytes_per_batch + hist_bytes + 8 * w.B + (w.B * w.V * 4 if mode == "noise" else 0)
+    return {"w": w, "bufs": bufs, "nbuf": nbuf, "kw": kw, "temps": temps, "tps": tps,
+            "bytes_per_batch": bytes_per_batch, "alg": alg}
+
+
+def time_steps(sampler, c, stream, steps: int, warmup: int, row_offset: int = 0, step0: int = 0):
+    """Warm-up, then `steps` sampler calls, each bracketed by CUDA events on
+    the launching stream.  Returns (total ms, per-call ms list)."""
+    import torch
+    w = c["w"]
+
+    def step(i):
+        return sampler(c["bufs"][i % c["nbuf"]], c["temps"], c["tps"], use_top_p=w.use_top_p, step=step0 + i,
+                       row_offset=row_offset, **c["kw"])
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    ev0.record(stream)
+    for i in range(steps):
+        per[i][0].record(stream)
+        step(warmup + i)
+        per[i][1].record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1), [a.elapsed_time(b) for a, b in per]
+
+
+def stats(ms_list):
+    v = np.asarray(ms_list) * 1e3
+    return {"median": float(np.median(v)), "p10": float(np.percentile(v, 10)), "p90": float(np.percentile(v, 90))}
+
+
+def traffic_record(cfg: int, mode: str):
+    """DRAM bytes per call measured by ncu for this configuration (a committed
+    summary, tagged with the kernels and the commit it was measured on)."""
+    prof = ROOT / "profiles" / f"traffic_config{cfg}_{mode}.json"
+    if not prof.exists():
+        return None, None
+    d = json.loads(prof.read_text())
+    return d.get("dram_bytes_per_call"), {k: d.get(k) for k in ("commit", "kernels", "source")}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--mode", default="philox", choices=["philox", "noise"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-extra-configs", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--vocab-sharded", action="store_true")
     args = ap.parse_args()
     if args.vocab_sharded and "--config" not in sys.argv:
@@ -249,13 +321,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if "--steps" not in sys.argv:
+            args.steps, args.warmup = 5, 3
         return run_reference(args, rank, world)
     if args.vocab_sharded:
         return run_vocab_sharded(args, rank, world, local)
 
     import torch
     import torch.distributed as dist
-    from qedge_b200 import workloads as W
     from qedge_b200.sampler import QESampler
 
     torch.cuda.set_device(local)
@@ -264,66 +337,30 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    w = W.CONFIGS[args.config]()
+    c = prepare_config(args.config, dev, args.mode)
+    w = c["w"]
     B, V = w.B, w.V
     row_offset = rank * B
-    esize = 4 if w.dtype == "f32" else 2
-    bytes_per_batch = B * V * esize
-    nbuf = max(2, int(np.ceil(2 * L2_BYTES / bytes_per_batch)) + 1)
-    base = W.to_device(w, dev)
-    bufs = [base] + [base.roll(shifts=i * 997, dims=1).contiguous() for i in range(1, nbuf)]
-    temps = torch.from_numpy(w.temperatures).to(dev)
-    tps = torch.from_numpy(w.top_ps).to(dev)
-    tks = torch.from_numpy(w.top_ks.astype(np.int32)).to(dev)
-    kw = {"top_ks": tks}
-    hist_bytes = 0
-    if w.history is not None:
-        kw.update(rep_penalties=torch.from_numpy(w.rep_penalties).to(dev),
-                  history=torch.from_numpy(w.history).to(dev),
-                  history_lens=torch.from_numpy(w.history_lens).to(dev))
-        hist_bytes = int(w.history_lens.sum()) * 4
-    noise = None
-    if args.mode == "noise":
-        noise = torch.from_numpy(W.exp_noise(B, V, 1)).to(dev)
     sampler = QESampler(seed=1234)
     stream = torch.cuda.current_stream(dev)
-
-    def step(i):
-        return sampler(bufs[i % nbuf], temps, tps, use_top_p=w.use_top_p, step=i,
-                       row_offset=row_offset, noise=noise, **kw)
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     clocks = ClockSampler(local)
     with clocks:
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        for i in range(args.steps):
-            per[i][0].record(stream)
-            step(args.warmup + i)
-            per[i][1].record(stream)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    total_ms = ev0.elapsed_time(ev1)
+        total_ms, launch_ms = time_steps(sampler, c, stream, args.steps, args.warmup, row_offset)
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
         dist.barrier()
     ms = total_ms / args.steps
-    launch_ms = [a.elapsed_time(b) for a, b in per]
 
-    # end-to-end through the public API: pinned host logits -> device, sample,
+    # end to end through the public API: pinned host logits -> device, sample,
     # ids -> host, every step
-    host = torch.empty_like(base, device="cpu").pin_memory()
-    host.copy_(base)
+    host = torch.empty_like(c["bufs"][0], device="cpu").pin_memory()
+    host.copy_(c["bufs"][0])
     out_host = torch.empty(B, dtype=torch.int64).pin_memory()
-    dbuf = torch.empty_like(base)
+    dbuf = torch.empty_like(c["bufs"][0])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -331,8 +368,8 @@ def main():
     e0.record(stream)
     for i in range(max(args.e2e_steps, 1)):
         dbuf.copy_(host, non_blocking=True)
-        ids = sampler(dbuf, temps, tps, use_top_p=w.use_top_p, step=10_000 + i,
-                      row_offset=row_offset, noise=noise, **kw)
+        ids = sampler(dbuf, c["temps"], c["tps"], use_top_p=w.use_top_p, step=10_000 + i,
+                      row_offset=row_offset, **c["kw"])
         out_host.copy_(ids, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -343,34 +380,58 @@ def main():
         e2e_ms = float(t.item())
 
     hbm, peak_kind = peaks()
-    alg_bytes = bytes_per_batch + hist_bytes + 8 * B + (B * V * 4 if noise is not None else 0)
-    med_launch = statistics.median(launch_ms)
-    achieved = alg_bytes / (med_launch * 1e-3) / 1e9
-    prof = ROOT / "profiles" / f"traffic_config{args.config}_{args.mode}.json"
-    traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch") if prof.exists() else None
+    st = stats(launch_ms)
+    achieved = c["alg"] / (st["median"] * 1e-6) / 1e9
+    traffic, traffic_src = traffic_record(args.config, args.mode)
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC if args.config == 3 else f"sampled rows/sec, config {args.config}",
             "value": world * B / (ms * 1e-3), "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "us_per_sample_step": ms * 1e3,
+            "us_per_sample_step": ms * 1e3, "us_per_call": st,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": {"bf16": "bf16", "f16": "f16", "f32": "f32"}[w.dtype] + " in, f32 math",
             "data": "synthetic",
             "config": {"workload": w.name, "B": B, "V": V, "noise": args.mode,
                        "parallelism": f"rows x{world} (no collective)",
-                       "l2": f"rotating {nbuf} logits buffers ({nbuf * bytes_per_batch / 2**20:.0f} MiB > 2x L2)"},
+                       "l2": f"rotating {c['nbuf']} logits buffers "
+                             f"({c['nbuf'] * c['bytes_per_batch'] / 2**20:.0f} MiB > 2x L2)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_kind": peak_kind,
                          "frac_of_8tbs": achieved / 8000.0, "traffic": traffic,
-                         "alg_bytes_per_launch": alg_bytes, "launch_us_median": med_launch * 1e3},
+                         "traffic_source": traffic_src,
+                         "alg_bytes_per_launch": c["alg"],
+                         "note": "achieved = algorithmic bytes / median time of one whole sampler call "
+                                 f"({LAUNCHES_PER_CALL} launches); the scan kernel is the dominant one"},
             "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": "rows/s",
-                    "h2d_bytes_per_step": bytes_per_batch, "d2h_bytes_per_step": 8 * B},
-            "gpu_launches": args.steps * (1 if os.environ.get("QE_SAMPLER_PATH", "auto") != "ref" else 5),
+                    "h2d_bytes_per_step": c["bytes_per_batch"], "d2h_bytes_per_step": 8 * B},
+            "gpu_launches": args.steps * LAUNCHES_PER_CALL,
             "clocks": clocks.summary(),
         }
+    del c
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_extra_configs:
+        # the other benchmark configurations: per-call time over >= 100 calls
+        extra = {}
+        for cfg in (1, 2, 4, 5):
+            if cfg == args.config:
+                continue
+            ce = prepare_config(cfg, dev, args.mode)
+            _, lm = time_steps(sampler, ce, stream, max(args.steps, 100), 10, 0, step0=50_000)
+            se = stats(lm)
+            ach = ce["alg"] / (se["median"] * 1e-6) / 1e9
+            extra[f"config{cfg}"] = {"workload": ce["w"].name, "B": ce["w"].B, "us_per_call": se,
+                                     "rows_per_s": ce["w"].B / (se["median"] * 1e-6),
+                                     "roofline_frac": ach / hbm, "alg_bytes_per_launch": ce["alg"]}
+            del ce
+            torch.cuda.empty_cache()
+            if not args.no_cpu_baseline:
+                extra[f"config{cfg}"]["cpu_baseline"] = cpu_baseline(cfg, rows=64)
+        line["configs"] = extra
+    if rank == 0:
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args.config, 16)
+            line["cpu_baseline"] = cpu_baseline(args.config)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

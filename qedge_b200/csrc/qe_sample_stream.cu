@@ -85,7 +85,8 @@ struct Params {
   TaskRec* trec;                // [B][tasks_row]
   float* emin;                  // [B][G] noise minimum per group (caller-noise mode)
   RowState* rstate;             // [B]
-  int* plist;                   // rows queued for the count kernel
+  int* plist;                   // [2][B] rows queued for the count kernel (per round)
+  int* rlist;                   // rows queued for the retry round
   int* flist;                   // rows queued for the finish kernel (row | kind << 28)
 };
 
@@ -327,7 +328,9 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     P.ctl->err = 0u;
-    P.ctl->n_pend = 0u;
+    P.ctl->n_pend[0] = 0u;
+    P.ctl->n_pend[1] = 0u;
+    P.ctl->n_retry = 0u;
     P.ctl->n_fin = 0u;
   }
   const long long task = (long long)blockIdx.x * (blockDim.x >> 5) + wib;
@@ -1144,9 +1147,15 @@ __device__ __noinline__ void exact_path(const Params& P, RowSm& sm, const RowP& 
   // the race over the kept set; its best is below 1/16 of its mass with
   // probability e^-16, and then everything it keeps is raced exactly
   const double mk = double(mass_keep) * (1.0 / 1099511627776.0);
-  const float theta = float(mk / S / 16.0);
+  float theta = float(mk / S / 16.0);
   race_row<T>(P, sm, rp, row, c0, Sf, theta, keep);
-  if (!(sm.ntop > 0 && sm.top[0].r >= theta)) race_row<T>(P, sm, rp, row, c0, Sf, 0.f, keep);
+  // the race's best is below theta with probability e^-16; each further
+  // round lowers theta 16-fold, the last one races every kept id
+#pragma unroll 1
+  for (int r = 1; r < 4 && !(sm.ntop > 0 && sm.top[0].r >= theta); ++r) {
+    theta = r < 3 ? theta * 0.0625f : 0.f;
+    race_row<T>(P, sm, rp, row, c0, Sf, theta, keep);
+  }
   if (sm.ntop == 0 && tid == 0) atomicOr(&P.ctl->err, 4u);
   write_row(P, row, sm.ntop > 0 ? sm.top[0].id : -1, QE_ROW_SLOW, nkeep);
 }
@@ -1466,12 +1475,23 @@ __device__ __forceinline__ void merge_top(DecSm& sm, const Top4& top) {
   __syncthreads();
 }
 
+// Ids a race may take: all, or (retry races) only those strictly ahead of
+// (x, id) in the order (x desc, id asc); every id at or after a candidate
+// that is outside the kept set is outside it too.
+struct Restr {
+  bool on;
+  float x;
+  int id;
+  __device__ __forceinline__ bool ok(float v, int i) const { return !on || v > x || (v == x && i < id); }
+};
+
 // One race round: every group whose noise bound can reach theta is expanded
-// exactly; sm.top gets the kTC best ratios, complete above theta.  Returns
-// false when a capacity ran out (the row then takes the exact path).
+// exactly; sm.top gets the kTC best ratios among the ids `rs_` allows,
+// complete above theta.  Returns false when a capacity ran out (the row
+// then takes the exact path).
 template <typename T>
 __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
-                           float theta) {
+                           float theta, const Restr& rr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ntask = P.tasks_row;
   const bool cnoise = P.a.noise != nullptr;
@@ -1482,6 +1502,7 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
   __syncthreads();
   for (int i = tid; i < ntask; i += kRowThreads) {
     const TaskRec& tr = sm.tr[i];
+    if (rr.on && tr.tmax < rr.x) continue;
     if (tr.bk0 >= lth && tr.bg0 != int(rp.s_gid)) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = tr.bg0;
     if (tr.bk1 >= lth && tr.bg1 != int(rp.s_gid)) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = tr.bg1;
     if (tr.bceil >= lth) {
@@ -1504,7 +1525,7 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
       const int64_t g = g0 + j;
       if (g == tr.bg0 || g == tr.bg1 || g == rp.s_gid) continue;
       const float gm = P.summ[size_t(row) * size_t(P.G) + size_t(g)].gmax;
-      if (!(gm > -INFINITY)) continue;
+      if (!(gm > -INFINITY) || (rr.on && gm < rr.x)) continue;
       const float lo = cnoise ? P.emin[size_t(row) * size_t(P.G) + size_t(g)] : emin_lower(group_min_word(rp.key, g));
       const float bk = lo > 0.f ? __fmul_rn(gm, rp.c1) - lg2_approx(lo) : INFINITY;
       if (bk >= lth) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = int(g);
@@ -1539,7 +1560,7 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
         const float e = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
         const int id = member_id(bid, m);
         const float E = __ldg(nz + id);
-        if (!(e >= __fmul_rn(pref, E))) continue;
+        if (!(e >= __fmul_rn(pref, E)) || !rr.ok(x[m], id)) continue;
         top.add(__fdiv_rn(__fdiv_rn(e, Sf), E), x[m], E, id);
       }
       continue;
@@ -1570,6 +1591,7 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
       if (m >= n) continue;
       const float e = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
       const int id = member_id(bid, m);
+      if (!rr.ok(x[m], id)) continue;
       if (m == am) {
         if (e >= __fmul_rn(pref, emin)) top.add(__fdiv_rn(__fdiv_rn(e, Sf), emin), x[m], emin, id);
       } else if (m == a2) {
@@ -1601,6 +1623,137 @@ __device__ __forceinline__ void push_fin(const Params& P, int row, unsigned kind
   P.flist[at] = int(unsigned(row) | (kind << 28));
 }
 
+// Race and kept-set test of a sampled row whose max and normaliser are
+// known.  Up to three rounds: the race (complete above 1/4, else above 1/16;
+// the best ratio is below those with probability e^-4 and e^-16), then the
+// test of its candidates in race order, from the task records and then the
+// group records.  A candidate outside the kept set restricts the next round
+// to the ids ahead of it.  Undecided candidates go to the count kernel of
+// `round`; rows still open after the rounds go to the finish kernel.
+template <typename T>
+__device__ void sample_rounds(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float Sf, double S,
+                              float thr_m, Restr rr, int round) {
+  const int tid = threadIdx.x;
+  const int ntask = P.tasks_row;
+  const int64_t V = P.a.vocab;
+  const float c0 = -u;
+  RowState* rs = P.rstate + row;
+  const double tpS = double(rp.tp) * S;
+  const GroupSum* gs = P.summ + size_t(row) * size_t(P.G);
+  const int G = int(P.G);
+#pragma unroll 1
+  for (int it = 0; it < 3; ++it) {
+    float theta = 0.25f;
+    bool ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta, rr);
+    if (ok && !(sm.ntop > 0 && sm.top[0].r >= theta)) {
+      theta = 0.0625f;
+      ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta, rr);
+    }
+    if (!ok || !(sm.ntop > 0 && sm.top[0].r >= theta)) break;
+    if (!rp.filtered) {
+      write_row(P, row, sm.top[0].id, 0, V);
+      return;
+    }
+    const int ntop = sm.ntop;
+    Restr nr = rr;
+#pragma unroll 1
+    for (int i = 0; i < ntop; ++i) {
+      const Cand c = sm.top[i];
+      if (!(c.r >= theta)) break;
+      const float e = qe_ex2_ftz(__fmaf_rn(c.x, rp.c1, c0));
+      bool in_p = true, in_k = true, out = false;
+      if (rp.m_on && __fdiv_rn(e, Sf) < thr_m) {
+        out = true;   // removed by min-p
+      } else {
+        double U = 0.0, Lm = 0.0;
+        long long N = 0, Lc = 0;
+        for (int t = tid; t < ntask; t += kRowThreads) {
+          const TaskRec& tr = sm.tr[t];
+          if (!(tr.tmax >= c.x)) continue;
+          U += tr.tsum * double(qe_ex2_ftz(__fsub_rn(__fmul_rn(tr.tmax, rp.c1), u)));
+          int64_t g0;
+          int ng;
+          task_groups(P, t, &g0, &ng);
+          N += (long long)ng * 32;
+        }
+        dsum2(sm, U, Lm, N, Lc);
+        in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
+        in_k = !rp.k_on || N - 1 < rp.k;
+        if (!(in_p && in_k)) {
+          // group level: eight record loads in flight per thread
+          U = 0.0; N = 0;
+          for (int gb = tid; gb < G; gb += kRowThreads * 8) {
+            GroupSum v[8];
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) {
+              const int g = gb + k2 * kRowThreads;
+              v[k2] = g < G ? gs[g] : GroupSum{-INFINITY, 0.f};
+            }
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) {
+              if (!(v[k2].gmax >= c.x)) continue;
+              U += double(v[k2].aux) * double(qe_ex2_ftz(__fsub_rn(__fmul_rn(v[k2].gmax, rp.c1), u)));
+              N += 32;
+              if (v[k2].gmax > c.x) {
+                Lm += double(qe_ex2_ftz(__fmaf_rn(v[k2].gmax, rp.c1, c0)));
+                Lc += 1;
+              }
+            }
+          }
+          dsum2(sm, U, Lm, N, Lc);
+          in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
+          in_k = !rp.k_on || N - 1 < rp.k;
+          out = (rp.p_on && Lm > tpS * (1.0 + 1e-6)) || (rp.k_on && Lc >= rp.k);
+        }
+      }
+      if (!out && in_p && in_k) {
+        write_row(P, row, c.id, 0, 0);
+        return;
+      }
+      if (out) {
+        if (!nr.on || c.x > nr.x || (c.x == nr.x && c.id < nr.id)) nr = Restr{true, c.x, c.id};
+        continue;
+      }
+      // undecided: the count kernel counts this and every later candidate
+      if (tid == 0) {
+        int n = 0;
+        for (int j = i; j < ntop; ++j) {
+          const Cand cj = sm.top[j];
+          if (!(cj.r >= theta)) break;
+          rs->cand[n] = cj;
+          rs->cmass[n] = 0ull;
+          rs->ccnt[n] = 0ull;
+          ++n;
+        }
+        rs->ncand = n;
+        rs->done = 0u;
+        rs->rx = nr.on ? nr.x : INFINITY;
+        rs->rid = nr.on ? nr.id : -1;
+        const unsigned at = atomicAdd(&P.ctl->n_pend[round], 1u);
+        P.plist[size_t(round) * size_t(P.a.batch) + at] = row;
+      }
+      return;
+    }
+    rr = nr;   // every candidate is outside the kept set
+  }
+  if (tid == 0) push_fin(P, row, kFinExact);
+}
+
+// Row parameters and the noise root of `row` into sm.rp (thread 0).
+__device__ __forceinline__ void load_row_params(const Params& P, DecSm& sm, int row) {
+  RowP r = row_params(P, row);
+  if (!P.a.noise && r.kind != kKindGreedy && r.kind != kKindArgmax) {
+    const NoiseRoot rt = noise_root(r.key, P.a.vocab);
+    int64_t gsd = -1;
+    int rm = 0;
+    token_group_p(P, rt.s, &gsd, &rm);
+    r.e_root = rt.e_root;
+    r.s_gid = gsd;
+    r.s_mem = rm;
+  }
+  sm.rp = r;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1611,19 +1764,7 @@ __global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_consta
   const int ntask = P.tasks_row;
   const TaskRec* trg = P.trec + size_t(row) * size_t(ntask);
   for (int i = tid; i < ntask; i += kRowThreads) sm.tr[i] = trg[i];
-  if (tid == 0) {
-    RowP r = row_params(P, row);
-    if (!P.a.noise && r.kind != kKindGreedy && r.kind != kKindArgmax) {
-      const NoiseRoot rt = noise_root(r.key, V);
-      int64_t gsd = -1;
-      int rm = 0;
-      token_group_p(P, rt.s, &gsd, &rm);
-      r.e_root = rt.e_root;
-      r.s_gid = gsd;
-      r.s_mem = rm;
-    }
-    sm.rp = r;
-  }
+  if (tid == 0) load_row_params(P, sm, row);
   __syncthreads();
   const RowP rp = sm.rp;
   const bool idx_mode = rp.kind == kKindGreedy || rp.kind == kKindArgmax;
@@ -1676,9 +1817,8 @@ __global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_consta
     write_row(P, row, first, status, rp.kind == kKindArgmax && fin ? 1 : 0);
     return;
   }
-  const float c0 = -u;
   const float Sf = float(S);
-  const float thr_m = rp.m_on ? __fmul_rn(rp.minp, __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xmax, rp.c1, c0)), Sf)) : 0.f;
+  const float thr_m = rp.m_on ? __fmul_rn(rp.minp, __fdiv_rn(qe_ex2_ftz(__fmaf_rn(xmax, rp.c1, -u)), Sf)) : 0.f;
   RowState* rs = P.rstate + row;
   if (tid == 0) {
     rs->xmax = xmax; rs->u = u; rs->Sf = Sf; rs->thr_m = thr_m; rs->S = S;
@@ -1689,115 +1829,54 @@ __global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_consta
     return;
   }
   if (rp.pen) hash_build(sm.hash, rp, V);
-  // race: complete above 1/4 (the best ratio of a race is below that with
-  // probability e^-4), then above 1/64
-  float theta = 0.25f;
-  bool ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta);
-  if (ok && !(sm.ntop > 0 && sm.top[0].r >= theta)) {
-    theta = 1.f / 64.f;
-    ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta);
-  }
-  if (!ok || !(sm.ntop > 0 && sm.top[0].r >= theta)) {
-    if (tid == 0) push_fin(P, row, kFinExact);
-    return;
-  }
-  if (!rp.filtered) {
-    write_row(P, row, sm.top[0].id, 0, V);
-    return;
-  }
-  // kept-set test of the candidates in race order: bounds from the task
-  // records, then from the group records of the tasks that can hold ids
-  // ahead; what they cannot settle is counted exactly by the count kernel
-  const int ntop = sm.ntop;
-  const double tpS = double(rp.tp) * S;
+  sample_rounds<T>(P, sm, rp, row, u, Sf, S, thr_m, Restr{false, 0.f, 0}, 0);
+}
+
+// Retry round: rows whose counted candidates were all outside the kept set
+// race again, restricted to the ids ahead of the best of them.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) retry_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  DecSm& sm = *reinterpret_cast<DecSm*>(smem_raw);
+  const unsigned nr = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_retry);
+  const int tid = threadIdx.x;
+  const int ntask = P.tasks_row;
 #pragma unroll 1
-  for (int i = 0; i < ntop; ++i) {
-    const Cand c = sm.top[i];
-    if (!(c.r >= theta)) break;
-    const float e = qe_ex2_ftz(__fmaf_rn(c.x, rp.c1, c0));
-    if (rp.m_on && __fdiv_rn(e, Sf) < thr_m) continue;   // removed by min-p
-    double U = 0.0, Lm = 0.0;
-    long long N = 0, Lc = 0;
-    for (int t = tid; t < ntask; t += kRowThreads) {
-      const TaskRec& tr = sm.tr[t];
-      if (!(tr.tmax >= c.x)) continue;
-      U += tr.tsum * double(qe_ex2_ftz(__fsub_rn(__fmul_rn(tr.tmax, rp.c1), u)));
-      int64_t g0;
-      int ng;
-      task_groups(P, t, &g0, &ng);
-      N += (long long)ng * 32;
-    }
-    dsum2(sm, U, Lm, N, Lc);
-    bool in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
-    bool in_k = !rp.k_on || N - 1 < rp.k;
-    bool out = false;
-    if (!(in_p && in_k)) {
-      // group level over the tasks whose max is at or above the candidate
-      U = 0.0; N = 0;
-      const int lane = tid & 31, warp = tid >> 5;
-      for (int t = warp; t < ntask; t += kRowWarps) {
-        if (!(sm.tr[t].tmax >= c.x)) continue;
-        int64_t g0;
-        int ng;
-        task_groups(P, t, &g0, &ng);
-        const GroupSum* gs = P.summ + size_t(row) * size_t(P.G) + size_t(g0);
-        for (int j = lane; j < ng; j += 32) {
-          const GroupSum sg = gs[j];
-          if (!(sg.gmax >= c.x)) continue;
-          const float ug = __fmul_rn(sg.gmax, rp.c1);
-          U += double(sg.aux) * double(qe_ex2_ftz(__fsub_rn(ug, u)));
-          N += 32;
-          if (sg.gmax > c.x) {
-            Lm += double(qe_ex2_ftz(__fmaf_rn(sg.gmax, rp.c1, c0)));
-            Lc += 1;
-          }
-        }
-      }
-      dsum2(sm, U, Lm, N, Lc);
-      in_p = !rp.p_on || U - double(e) <= tpS * (1.0 - 1e-6);
-      in_k = !rp.k_on || N - 1 < rp.k;
-      out = (rp.p_on && Lm > tpS * (1.0 + 1e-6)) || (rp.k_on && Lc >= rp.k);
-    }
-    if (in_p && in_k) {
-      write_row(P, row, c.id, 0, 0);
-      return;
-    }
-    if (out) continue;
-    // undecided: the count kernel counts this and every later candidate
-    if (tid == 0) {
-      int n = 0;
-      for (int j = i; j < ntop; ++j) {
-        const Cand cj = sm.top[j];
-        if (!(cj.r >= theta)) break;
-        rs->cand[n] = cj;
-        rs->cmass[n] = 0ull;
-        rs->ccnt[n] = 0ull;
-        ++n;
-      }
-      rs->ncand = n;
-      const unsigned at = atomicAdd(&P.ctl->n_pend, 1u);
-      P.plist[at] = row;
-    }
-    return;
+  for (unsigned li = blockIdx.x; li < nr; li += gridDim.x) {
+    const int row = P.rlist[li];
+    const TaskRec* trg = P.trec + size_t(row) * size_t(ntask);
+    for (int i = tid; i < ntask; i += kRowThreads) sm.tr[i] = trg[i];
+    if (tid == 0) load_row_params(P, sm, row);
+    __syncthreads();
+    const RowP rp = sm.rp;
+    const RowState* rs = P.rstate + row;
+    const float u = rs->u, Sf = rs->Sf, thr_m = rs->thr_m;
+    const double S = rs->S;
+    const Restr rr{true, rs->rx, rs->rid};
+    if (rp.pen) hash_build(sm.hash, rp, P.a.vocab);
+    sample_rounds<T>(P, sm, rp, row, u, Sf, S, thr_m, rr, 1);
+    __syncthreads();
   }
-  if (tid == 0) push_fin(P, row, kFinExact);   // every candidate is outside the kept set
 }
 
 // ---------------------------------------------------------------- 3. count kernel
 // Exact count and mass of the ids ahead of each pending candidate, one warp
 // per (pending row, scan task); the warp that completes a row decides it.
+// A row whose candidates are all outside the kept set goes to the retry
+// round (from the first round) or to the finish kernel (from the retry round).
 template <typename T>
-__global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constant__ Params P, int round) {
   __shared__ uint32_t pen_bits[kSumThreads / 32][64];
-  const unsigned npend = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_pend);
+  const unsigned npend = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_pend[round]);
   if (npend == 0u) return;
+  const int* plist = P.plist + size_t(round) * size_t(P.a.batch);
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const long long items = (long long)npend * P.tasks_row;
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
   const KernelArgs& a = P.a;
 #pragma unroll 1
   for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + wib; item < items; item += nw) {
-    const int row = P.plist[item / P.tasks_row];
+    const int row = plist[item / P.tasks_row];
     const int t = int(item % P.tasks_row);
     RowState* rs = P.rstate + row;
     const int nc = rs->ncand;
@@ -1892,19 +1971,32 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
         const float Sf = rs->Sf, thr_m = rs->thr_m;
         const bool m_on = a.min_ps && a.min_ps[row] > 0.f;
         long long win = -1;
+        float bx = rs->rx;
+        int bid2 = rs->rid;
         for (int i = 0; i < nc; ++i) {
           const unsigned long long mm = atomicAdd(&rs->cmass[i], 0ull);
           const unsigned long long cc = atomicAdd(&rs->ccnt[i], 0ull);
-          if (m_on && __fdiv_rn(qe_ex2_ftz(__fmaf_rn(cand[i].x, c1, c0)), Sf) < thr_m) continue;
-          if ((!k_on || (long long)cc < kraw) && mm <= tfix) {
+          const bool in = !(m_on && __fdiv_rn(qe_ex2_ftz(__fmaf_rn(cand[i].x, c1, c0)), Sf) < thr_m) &&
+                          (!k_on || (long long)cc < kraw) && mm <= tfix;
+          if (in) {
             win = cand[i].id;
             break;
+          }
+          // outside: the ids at and after it are outside too
+          if (bid2 < 0 || cand[i].x > bx || (cand[i].x == bx && cand[i].id < bid2)) {
+            bx = cand[i].x;
+            bid2 = cand[i].id;
           }
         }
         if (win >= 0) {
           a.out_ids[row] = win;
           if (a.out_status) a.out_status[row] = 0;
           if (a.out_kept) a.out_kept[row] = 0;
+        } else if (round == 0) {
+          rs->rx = bx;
+          rs->rid = bid2;
+          const unsigned at = atomicAdd(&P.ctl->n_retry, 1u);
+          P.rlist[at] = row;
         } else {
           push_fin(P, row, kFinExact);
         }
@@ -1975,6 +2067,8 @@ cudaError_t prepare() {
   cudaError_t e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(RowSm)));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decide_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmFull));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(retry_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmFull));
   return e;
 }
 
@@ -2003,7 +2097,9 @@ void launch_all(const Params& P, unsigned g1, int wpc, unsigned g2, size_t dec_s
                 cudaStream_t stream) {
   scan_kernel<T><<<g1, wpc * 32, 0, stream>>>(P);
   decide_kernel<T><<<g2, kRowThreads, dec_smem, stream>>>(P);
-  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P);
+  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P, 0);
+  retry_kernel<T><<<g4, kRowThreads, dec_smem, stream>>>(P);
+  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P, 1);
   finish_kernel<T><<<g4, kRowThreads, sizeof(RowSm), stream>>>(P);
 }
 
@@ -2063,6 +2159,7 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   P.emin = reinterpret_cast<float*>(base + L.emin);
   P.rstate = reinterpret_cast<RowState*>(base + L.rstate);
   P.plist = reinterpret_cast<int*>(base + L.plist);
+  P.rlist = reinterpret_cast<int*>(base + L.rlist);
   P.flist = reinterpret_cast<int*>(base + L.flist);
   // scan: one warp per task; narrower CTAs when there are few tasks, so that
   // they spread over the SMs

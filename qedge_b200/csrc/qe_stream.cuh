@@ -62,13 +62,15 @@ struct Cand {
   int id;
 };
 
-// Per-row state handed from the decide kernel to the count and finish
-// kernels.
+// Per-row state handed from the decide kernel to the count, retry and
+// finish kernels.
 struct alignas(16) RowState {
   float xmax, u, Sf, thr_m;   // row max, RN(xmax c1), float(S), min-p threshold on p
   double S;                   // softmax normaliser relative to 2^u
   int ncand;                  // candidates still to test (count kernel)
   unsigned int done;          // tasks counted so far (count kernel)
+  float rx;                   // retry race: only ids strictly ahead of (rx, rid) in the order
+  int rid;
   Cand cand[kTC];
   unsigned long long cmass[kTC];   // mass ahead of each candidate, fixed point 2^-40
   unsigned long long ccnt[kTC];    // ids ahead of each candidate
@@ -77,9 +79,10 @@ struct alignas(16) RowState {
 // Launch-wide words, zeroed by the scan kernel.
 struct alignas(128) Ctl {
   unsigned int err;          // 4: a race found no candidate (cannot happen on finite rows)
-  unsigned int n_pend;       // rows queued for the count kernel
+  unsigned int n_pend[2];    // rows queued for the count kernel (first and retry round)
+  unsigned int n_retry;      // rows queued for the retry round (all candidates outside the kept set)
   unsigned int n_fin;        // rows queued for the finish kernel
-  unsigned int pad[29];
+  unsigned int pad[27];
 };
 
 // Finish-list entries: row | kind << 28.
@@ -90,7 +93,7 @@ struct Layout {
   int64_t G;                 // groups per row
   int tasks;                 // scan tasks per row
   int tpw;                   // tiles per task
-  size_t summ, trec, emin, rstate, plist, flist, total;
+  size_t summ, trec, emin, rstate, plist, rlist, flist, total;
 };
 
 inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
@@ -134,7 +137,8 @@ inline Layout make_layout(int64_t B, int64_t V, int esize) {
   L.emin = align256(L.trec + b * size_t(L.tasks) * sizeof(TaskRec));
   L.rstate = align256(L.emin + b * size_t(L.G) * sizeof(float));
   L.plist = align256(L.rstate + b * sizeof(RowState));
-  L.flist = align256(L.plist + b * sizeof(int));
+  L.rlist = align256(L.plist + 2 * b * sizeof(int));
+  L.flist = align256(L.rlist + b * sizeof(int));
   L.total = align256(L.flist + b * sizeof(int));
   return L;
 }
