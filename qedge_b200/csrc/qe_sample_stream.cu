@@ -48,6 +48,7 @@ namespace st {
 using fz::key_to_float;
 using fz::ordered_key;
 using fz::rbetter;
+using fz::smem_u32;
 
 // ---------------------------------------------------------------- small helpers
 __device__ __forceinline__ float lg2_approx(float x) {
@@ -241,18 +242,43 @@ __device__ __forceinline__ int first_member(const float x[32], float v) {
   return f;
 }
 
-// The same two reductions on 32 packed 16-bit values (word i holds members
-// 2i and 2i+1), in group_sum's order.
+// Packed fp32 pairs (Blackwell f32x2 FMA / add: two IEEE operations each, so
+// the results are those of the scalar group_sum).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// group_sum on 32 packed 16-bit values (word i holds members 2i and 2i+1),
+// in its order: chains (s0, s1) and (s2, s3) as f32x2 pairs.
 template <typename T>
 __device__ __forceinline__ float group_sum_packed(const uint32_t w[16], float c1, float c0) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  const unsigned long long cc1 = pk2(c1, c1), cc0 = pk2(c0, c0);
+  unsigned long long s01 = 0ull, s23 = 0ull;   // (s0, s1), (s2, s3): +0.0f pairs
 #pragma unroll
   for (int i = 0; i < 16; i += 2) {
-    s0 += qe_ex2_ftz(__fmaf_rn(Cvt<T>::lo(w[i]), c1, c0));
-    s1 += qe_ex2_ftz(__fmaf_rn(Cvt<T>::hi(w[i]), c1, c0));
-    s2 += qe_ex2_ftz(__fmaf_rn(Cvt<T>::lo(w[i + 1]), c1, c0));
-    s3 += qe_ex2_ftz(__fmaf_rn(Cvt<T>::hi(w[i + 1]), c1, c0));
+    float a, b;
+    upk2(fma2(pk2(Cvt<T>::lo(w[i]), Cvt<T>::hi(w[i])), cc1, cc0), a, b);
+    s01 = add2(s01, pk2(qe_ex2_ftz(a), qe_ex2_ftz(b)));
+    upk2(fma2(pk2(Cvt<T>::lo(w[i + 1]), Cvt<T>::hi(w[i + 1])), cc1, cc0), a, b);
+    s23 = add2(s23, pk2(qe_ex2_ftz(a), qe_ex2_ftz(b)));
   }
+  float s0, s1, s2, s3;
+  upk2(s01, s0, s1);
+  upk2(s23, s2, s3);
   return (s0 + s1) + (s2 + s3);
 }
 template <typename T>
@@ -322,28 +348,52 @@ struct Top3 {
   }
 };
 
+// cp.async (16 bytes, L2 only) and its group waits.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kScanRounds = 2;   // rounds of two tiles per task whose copies are issued up front (tpw <= 4)
+constexpr size_t kScanSmem = size_t(kSumThreads / 32) * kScanRounds * 2 * 4 * 32 * sizeof(uint4);
+
+// Scan task t of `row` by one warp: GroupSums of its groups, its TaskRec.
 template <typename T>
-__global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_constant__ Params P) {
-  __shared__ uint32_t pen_bits[kSumThreads / 32][64];
+__device__ __forceinline__ void scan_task(const Params& P, int row, int t, uint4* sbuf, uint32_t (*pen_bits)[64]) {
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    P.ctl->err = 0u;
-    P.ctl->n_pend[0] = 0u;
-    P.ctl->n_pend[1] = 0u;
-    P.ctl->n_retry = 0u;
-    P.ctl->n_fin = 0u;
-  }
-  const long long task = (long long)blockIdx.x * (blockDim.x >> 5) + wib;
-  if (task >= (long long)P.a.batch * P.tasks_row) return;   // the whole warp
-  const int row = int(task / P.tasks_row), t = int(task % P.tasks_row);
   int s = 0;
-#pragma unroll 1
-  while (s + 1 < kNumSlices && P.tbase[s + 1] <= t) ++s;
+#pragma unroll
+  for (int step = 8; step > 0; step >>= 1)
+    if (s + step < kNumSlices && P.tbase[s + step] <= t) s += step;
   const int tile0 = (t - P.tbase[s]) * P.tpw;
   const int ntile = min(P.tpw, P.snt[s] - tile0);
   const int64_t sa = P.sstart[s];
   const int L = int(P.sstart[s + 1] - sa);
   const KernelArgs& a = P.a;
+  const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
+  // 16-bit rows: every full tile of the task on its way into shared memory
+  // before any arithmetic (one commit group per round of two tiles)
+  constexpr bool k16 = sizeof(T) == 2;
+  const bool cp_ok = k16 && P.vec_ok && P.tpw <= 2 * kScanRounds;
+  uint4* wb = sbuf + size_t(wib) * (kScanRounds * 2 * 4 * 32);
+  if (cp_ok) {
+#pragma unroll
+    for (int r = 0; r < kScanRounds; ++r) {
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        const int tl = 2 * r + tt;
+        const int tile = tile0 + tl;
+        if (tl < ntile && tile * kTile + kTile <= L) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            cp_async16(wb + ((r * 2 + tt) * 4 + b) * 32 + lane, src + size_t(tile * kTile + b * 256 + lane * 8) * 2);
+        }
+      }
+      cp_async_commit();
+    }
+  }
   const float temp = a.temperatures[row];
   const long long k = a.top_ks ? (long long)a.top_ks[row] : 0;
   const bool idx_mode = (a.flags & QE_FLAG_ALL_GREEDY) || temp <= kGreedyEps || (k == 1 && a.vocab > 1);
@@ -358,39 +408,23 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
   const bool pen = hl > 0 && !(rpen == 1.f);
   const int32_t* hist = pen ? a.history + row * a.history_ld : nullptr;
   const NoiseKey key = make_noise_key(row_seed(a, row), a.step_ptr ? *a.step_ptr : a.step, a.row_offset + row);
-  const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
   const int64_t g_first = P.gbase[s] + int64_t(tile0) * 32;   // global id of the task's first group
   GroupSum* out = P.summ + size_t(row) * size_t(P.G) + size_t(g_first);
   const float* nzrow = a.noise ? a.noise + size_t(row) * size_t(a.noise_ld) + size_t(sa) : nullptr;
   // per-lane task state: NaN-aware max, sum in the lane's running scale, bound keys
-  float lmax = -INFINITY, lu = -INFINITY;
-  double lsum = 0.0;
+  float lmax = -INFINITY, lu = -INFINITY, lsum = 0.f;
   Top3 top;
   top.init();
-  constexpr int kStep = sizeof(T) == 2 ? 2 : 1;   // tiles per load round
+  constexpr int kStep = k16 ? 2 : 1;   // tiles per round
 #pragma unroll 1
-  for (int tp = 0; tp < ntile; tp += kStep) {
+  for (int tp = 0, r = 0; tp < ntile; tp += kStep, ++r) {
     const int nt = min(kStep, ntile - tp);
     const int tbase = tile0 + tp;
-    if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tbase, nt, L);
-    // 16-bit rows: every full tile's loads in flight before any arithmetic
-    uint32_t wv[2][16];
-    bool fast[2] = {false, false};
-    if constexpr (sizeof(T) == 2) {
-#pragma unroll
-      for (int tt = 0; tt < 2; ++tt) {
-        const int tile = tbase + tt;
-        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
-        fast[tt] = tt < nt && pb == 0u && tile * kTile + kTile <= L && P.vec_ok;
-        if (fast[tt]) {
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + size_t(tile * kTile + b * 256 + lane * 8) * 2));
-            wv[tt][4 * b] = q.x; wv[tt][4 * b + 1] = q.y; wv[tt][4 * b + 2] = q.z; wv[tt][4 * b + 3] = q.w;
-          }
-        }
-      }
+    if (cp_ok) {
+      if (r == 0) cp_async_wait<kScanRounds - 1>();
+      else cp_async_wait<0>();
     }
+    if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tbase, nt, L);
     // group-minimum noise words of the round's groups (one Philox call per four)
     uint32_t wmin[2] = {0u, 0u};
     if (!idx_mode && !a.noise) {
@@ -409,30 +443,50 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
     for (int tt = 0; tt < 2; ++tt) {
       if (tt >= nt) break;
       const int tile = tbase + tt;
-      GroupSum r;
+      const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
+      const bool in_smem = cp_ok && tile * kTile + kTile <= L;
+      GroupSum r_;
       bool done = false;
-      if constexpr (sizeof(T) == 2) {
-        if (fast[tt]) {
-          done = true;
-          const uint32_t* w = wv[tt];
-          const uint32_t m0 = Cvt<T>::max2(Cvt<T>::max2(w[0], w[1]), Cvt<T>::max2(w[2], w[3]));
-          const uint32_t m1 = Cvt<T>::max2(Cvt<T>::max2(w[4], w[5]), Cvt<T>::max2(w[6], w[7]));
-          const uint32_t m2 = Cvt<T>::max2(Cvt<T>::max2(w[8], w[9]), Cvt<T>::max2(w[10], w[11]));
-          const uint32_t m3 = Cvt<T>::max2(Cvt<T>::max2(w[12], w[13]), Cvt<T>::max2(w[14], w[15]));
-          const uint32_t mm = Cvt<T>::max2(Cvt<T>::max2(m0, m1), Cvt<T>::max2(m2, m3));
-          const float lo = Cvt<T>::lo(mm), hi = Cvt<T>::hi(mm);
-          const float gmax = (lo != lo || hi != hi) ? __int_as_float(0x7FFFFFFF) : fmaxf(lo, hi);
-          r.gmax = gmax;
-          if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
-            r.aux = __int_as_float(first_member_packed<T>(w, gmax));
-          else
-            r.aux = gmax > -INFINITY ? group_sum_packed<T>(w, c1, -__fmul_rn(gmax, c1)) : 0.f;
+      uint32_t w[16];
+      if constexpr (k16) {
+        if (in_smem) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const uint4 q = wb[((r * 2 + tt) * 4 + b) * 32 + lane];
+            w[4 * b] = q.x; w[4 * b + 1] = q.y; w[4 * b + 2] = q.z; w[4 * b + 3] = q.w;
+          }
+          if (pb == 0u) {
+            done = true;
+            const uint32_t m0 = Cvt<T>::max2(Cvt<T>::max2(w[0], w[1]), Cvt<T>::max2(w[2], w[3]));
+            const uint32_t m1 = Cvt<T>::max2(Cvt<T>::max2(w[4], w[5]), Cvt<T>::max2(w[6], w[7]));
+            const uint32_t m2 = Cvt<T>::max2(Cvt<T>::max2(w[8], w[9]), Cvt<T>::max2(w[10], w[11]));
+            const uint32_t m3 = Cvt<T>::max2(Cvt<T>::max2(w[12], w[13]), Cvt<T>::max2(w[14], w[15]));
+            const uint32_t mm = Cvt<T>::max2(Cvt<T>::max2(m0, m1), Cvt<T>::max2(m2, m3));
+            const float lo = Cvt<T>::lo(mm), hi = Cvt<T>::hi(mm);
+            const float gmax = (lo != lo || hi != hi) ? __int_as_float(0x7FFFFFFF) : fmaxf(lo, hi);
+            r_.gmax = gmax;
+            if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
+              r_.aux = __int_as_float(first_member_packed<T>(w, gmax));
+            else
+              r_.aux = gmax > -INFINITY ? group_sum_packed<T>(w, c1, -__fmul_rn(gmax, c1)) : 0.f;
+          }
         }
       }
       if (!done) {
         float x[32];
-        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
-        load_members<T>(P, src, tile, lane, L, x);
+        if constexpr (k16) {
+          if (in_smem) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              x[2 * i] = Cvt<T>::lo(w[i]);
+              x[2 * i + 1] = Cvt<T>::hi(w[i]);
+            }
+          } else {
+            load_members<T>(P, src, tile, lane, L, x);
+          }
+        } else {
+          load_members<T>(P, src, tile, lane, L, x);
+        }
         if (pb) {
 #pragma unroll
           for (int m = 0; m < 32; ++m)
@@ -441,19 +495,19 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
         float gmax = x[0];
 #pragma unroll
         for (int m = 1; m < 32; ++m) gmax = fmax_nan(gmax, x[m]);
-        r.gmax = gmax;
+        r_.gmax = gmax;
         // rows that only need the max's position, and groups whose softmax terms
         // are not finite (the row then falls back to the greedy id), keep the
         // position of the group's max instead of its sum
         if (idx_mode || gmax != gmax || (gmax > -INFINITY && !finite_f(__fmul_rn(gmax, c1))))
-          r.aux = __int_as_float(first_member(x, gmax));
+          r_.aux = __int_as_float(first_member(x, gmax));
         else
-          r.aux = gmax > -INFINITY ? group_sum(x, c1, -__fmul_rn(gmax, c1)) : 0.f;
+          r_.aux = gmax > -INFINITY ? group_sum(x, c1, -__fmul_rn(gmax, c1)) : 0.f;
       }
-      const int64_t gl = int64_t(tp + tt) * 32 + lane;   // group index inside the task
-      out[gl] = r;
-      lmax = fmax_nan(lmax, r.gmax);
-      if (idx_mode || !(r.gmax > -INFINITY) || !finite_f(__fmul_rn(r.gmax, c1))) continue;
+      const int gl = (tp + tt) * 32 + lane;   // group index inside the task
+      out[gl] = r_;
+      lmax = fmax_nan(lmax, r_.gmax);
+      if (idx_mode || !(r_.gmax > -INFINITY) || !finite_f(__fmul_rn(r_.gmax, c1))) continue;
       // the group's lower bound of its noise minimum
       float lo;
       if (nzrow) {
@@ -475,16 +529,17 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
       } else {
         lo = emin_lower(wmin[tt]);
       }
-      const float ug = __fmul_rn(r.gmax, c1);
+      const float ug = __fmul_rn(r_.gmax, c1);
       if (ug > lu) {
-        lsum = lsum * double(qe_ex2_ftz(__fsub_rn(lu, ug))) + double(r.aux);
+        lsum = __fmaf_rn(lsum, qe_ex2_ftz(__fsub_rn(lu, ug)), r_.aux);
         lu = ug;
       } else {
-        lsum += double(r.aux) * double(qe_ex2_ftz(__fsub_rn(ug, lu)));
+        lsum = __fmaf_rn(r_.aux, qe_ex2_ftz(__fsub_rn(ug, lu)), lsum);
       }
       top.add(lo > 0.f ? ug - lg2_approx(lo) : INFINITY, int(g_first + gl));
     }
   }
+  if (cp_ok) cp_async_wait<0>();   // no copy outlives the warp (tiles past the task's end were not issued)
   // task record: warp reductions
   const uint32_t kmax = __reduce_max_sync(0xFFFFFFFFu, nan_key(lmax));
   const float tmax = kmax == 0xFFFFFFFFu ? __int_as_float(0x7FFFFFFF) : key_to_float(kmax);
@@ -493,7 +548,7 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
   double ts = 0.0;
   if (!idx_mode) {
     const float ut = __fmul_rn(tmax, c1);
-    if (lu > -INFINITY && finite_f(ut)) ts = lsum * double(qe_ex2_ftz(__fsub_rn(lu, ut)));
+    if (lu > -INFINITY && finite_f(ut)) ts = double(lsum) * double(qe_ex2_ftz(__fsub_rn(lu, ut)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ts += __shfl_xor_sync(0xFFFFFFFFu, ts, o);
   }
@@ -518,6 +573,26 @@ __global__ void __launch_bounds__(kSumThreads, 2) scan_kernel(const __grid_const
   tr.bg0 = kv[0] > -INFINITY ? kg[0] : -1;
   tr.bg1 = kv[1] > -INFINITY ? kg[1] : -1;
   if (lane == 0) P.trec[size_t(row) * size_t(P.tasks_row) + size_t(t)] = tr;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSumThreads, 3) scan_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(16) uint4 sbuf[];   // [warp][round][tile][block][lane]
+  __shared__ uint32_t pen_bits[kSumThreads / 32][64];
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    P.ctl->err = 0u;
+    P.ctl->n_pend[0] = 0u;
+    P.ctl->n_pend[1] = 0u;
+    P.ctl->n_retry = 0u;
+    P.ctl->n_fin = 0u;
+  }
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= P.tasks_row) return;   // the whole warp
+#pragma unroll 1
+  for (int row = blockIdx.y; row < int(P.a.batch); row += gridDim.y) {
+    scan_task<T>(P, row, t, sbuf, pen_bits);
+    __syncwarp();
+  }
 }
 
 
@@ -874,18 +949,24 @@ __device__ __noinline__ void race_row(const Params& P, RowSm& sm, const RowP& rp
       const int i2 = int(select_index32(wd.w, uint32_t(n - 1)));
       a2 = i2 < a ? i2 : i2 + 1;
     }
-    // the noise-minimum and second members exactly; the others bounded by
-    // RN(p/E2) first, their token noise only when that reaches theta
+    // the noise-minimum and second members exactly (selected without
+    // branches); the others bounded by their ratio with E2 first, their token
+    // noise only when that can reach theta
+    const float pre2 = __fmul_rn(__fmul_rn(__fmul_rn(theta, Sf), e2), 1.f - 1e-5f);
+    float xa = -INFINITY, xb = -INFINITY;
     uint32_t need = 0u;
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
-      const int id = member_id(bid, m);
-      if (m >= n || !keep(x[m], id)) continue;
-      const float p = __fdiv_rn(qe_ex2_ftz(__fmaf_rn(x[m], c1, c0)), Sf);
-      if (m == a) top.add(__fdiv_rn(p, emin), x[m], emin, id);
-      else if (m == a2) top.add(__fdiv_rn(p, e2), x[m], e2, id);
-      else if (__fdiv_rn(p, e2) >= theta) need |= 1u << m;
+      xa = m == a ? x[m] : xa;
+      xb = m == a2 ? x[m] : xb;
+      const bool pass = m < n && m != a && m != a2 && qe_ex2_ftz(__fmaf_rn(x[m], c1, c0)) >= pre2 &&
+                        keep(x[m], member_id(bid, m));
+      need |= pass ? (1u << m) : 0u;
     }
+    if (a < n && keep(xa, member_id(bid, a)))
+      top.add(__fdiv_rn(__fdiv_rn(qe_ex2_ftz(__fmaf_rn(xa, c1, c0)), Sf), emin), xa, emin, member_id(bid, a));
+    if (a2 >= 0 && a2 < n && keep(xb, member_id(bid, a2)))
+      top.add(__fdiv_rn(__fdiv_rn(qe_ex2_ftz(__fmaf_rn(xb, c1, c0)), Sf), e2), xb, e2, member_id(bid, a2));
 #pragma unroll 1
     while (need) {
       const int m = __ffs(need) - 1;
@@ -1490,7 +1571,7 @@ struct Restr {
 // complete above theta.  Returns false when a capacity ran out (the row
 // then takes the exact path).
 template <typename T>
-__device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
+__device__ __noinline__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
                            float theta, const Restr& rr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ntask = P.tasks_row;
@@ -1521,14 +1602,24 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
     int64_t g0;
     int ng;
     task_groups(P, t, &g0, &ng);
-    for (int j = lane; j < ng; j += 32) {
+    float gms[4];
+    for (int j0 = 0; j0 < ng; j0 += 128) {
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) {
+        const int j = j0 + k2 * 32 + lane;
+        gms[k2] = j < ng ? P.summ[size_t(row) * size_t(P.G) + size_t(g0 + j)].gmax : -INFINITY;
+      }
+#pragma unroll
+     for (int k2 = 0; k2 < 4; ++k2) {
+      const int j = j0 + k2 * 32 + lane;
       const int64_t g = g0 + j;
-      if (g == tr.bg0 || g == tr.bg1 || g == rp.s_gid) continue;
-      const float gm = P.summ[size_t(row) * size_t(P.G) + size_t(g)].gmax;
+      const float gm = gms[k2];
+      if (j >= ng || g == tr.bg0 || g == tr.bg1 || g == rp.s_gid) continue;
       if (!(gm > -INFINITY) || (rr.on && gm < rr.x)) continue;
       const float lo = cnoise ? P.emin[size_t(row) * size_t(P.G) + size_t(g)] : emin_lower(group_min_word(rp.key, g));
       const float bk = lo > 0.f ? __fmul_rn(gm, rp.c1) - lg2_approx(lo) : INFINITY;
       if (bk >= lth) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = int(g);
+     }
     }
   }
   __syncthreads();
@@ -1585,20 +1676,28 @@ __device__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, 
       a2 = i2 < am ? i2 : i2 + 1;
     }
     const float pre2 = __fmul_rn(pref, e2);
+    // the noise-minimum and second members exactly (selected without
+    // branches: the members differ from lane to lane); every other member
+    // only marked when RN(p/E2) can reach theta
+    float xa = -INFINITY, xb = -INFINITY;
     uint32_t need = 0u;
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
-      if (m >= n) continue;
-      const float e = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
-      const int id = member_id(bid, m);
-      if (!rr.ok(x[m], id)) continue;
-      if (m == am) {
-        if (e >= __fmul_rn(pref, emin)) top.add(__fdiv_rn(__fdiv_rn(e, Sf), emin), x[m], emin, id);
-      } else if (m == a2) {
-        if (e >= pre2) top.add(__fdiv_rn(__fdiv_rn(e, Sf), e2), x[m], e2, id);
-      } else if (e >= pre2) {
-        need |= 1u << m;
-      }
+      xa = m == am ? x[m] : xa;
+      xb = m == a2 ? x[m] : xb;
+      const bool pass = m < n && m != am && m != a2 && qe_ex2_ftz(__fmaf_rn(x[m], c1, c0)) >= pre2 &&
+                        rr.ok(x[m], member_id(bid, m));
+      need |= pass ? (1u << m) : 0u;
+    }
+    if (am < n) {
+      const int id = member_id(bid, am);
+      const float e = qe_ex2_ftz(__fmaf_rn(xa, c1, c0));
+      if (rr.ok(xa, id) && e >= __fmul_rn(pref, emin)) top.add(__fdiv_rn(__fdiv_rn(e, Sf), emin), xa, emin, id);
+    }
+    if (a2 >= 0 && a2 < n) {
+      const int id = member_id(bid, a2);
+      const float e = qe_ex2_ftz(__fmaf_rn(xb, c1, c0));
+      if (rr.ok(xb, id) && e >= pre2) top.add(__fdiv_rn(__fdiv_rn(e, Sf), e2), xb, e2, id);
     }
 #pragma unroll 1
     while (need) {
@@ -1631,7 +1730,7 @@ __device__ __forceinline__ void push_fin(const Params& P, int row, unsigned kind
 // to the ids ahead of it.  Undecided candidates go to the count kernel of
 // `round`; rows still open after the rounds go to the finish kernel.
 template <typename T>
-__device__ void sample_rounds(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float Sf, double S,
+__device__ __noinline__ void sample_rounds(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float Sf, double S,
                               float thr_m, Restr rr, int round) {
   const int tid = threadIdx.x;
   const int ntask = P.tasks_row;
@@ -1907,16 +2006,21 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
     const int L = int(P.sstart[s + 1] - sa);
     const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
     const GroupSum* gs = P.summ + size_t(row) * size_t(P.G) + size_t(P.gbase[s] + int64_t(tile0) * 32);
-    unsigned long long ms[kTC] = {0ull, 0ull, 0ull, 0ull}, ct[kTC] = {0ull, 0ull, 0ull, 0ull};
+    // per candidate: mass (fp32 per lane, then 2^-40 fixed point) and count
+    // of the ids strictly ahead of it
+    float msf[kTC] = {0.f, 0.f, 0.f, 0.f};
+    unsigned long long ms[kTC], ct[kTC] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll 1
     for (int tp = 0; tp < ntile; tp += 2) {
       const int nt = min(2, ntile - tp);
       if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tile0 + tp, nt, L);
+      float gm2[2];
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) gm2[tt] = tt < nt ? gs[(tp + tt) * 32 + lane].gmax : -INFINITY;
 #pragma unroll 1
       for (int tt = 0; tt < nt; ++tt) {
         const int tile = tile0 + tp + tt;
-        const GroupSum sg = gs[(tp + tt) * 32 + lane];
-        if (!(sg.gmax >= xlo)) continue;
+        if (!(gm2[tt] >= xlo)) continue;
         float x[32];
         load_members<T>(P, src, tile, lane, L, x);
         const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
@@ -1926,22 +2030,29 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
             if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
         }
         const int bid = int(sa) + tile * kTile + lane * 8;
+        float e[32];
 #pragma unroll
-        for (int m = 0; m < 32; ++m) {
-          const float v = x[m];
-          if (!(v >= xlo)) continue;
-          const int id = member_id(bid, m);
-          const unsigned long long f = efix(v, c1, c0);
+        for (int m = 0; m < 32; ++m) e[m] = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
 #pragma unroll
-          for (int i = 0; i < kTC; ++i) {
-            if (v > cand[i].x || (v == cand[i].x && id < cand[i].id)) {
-              ms[i] += f;
-              ct[i] += 1ull;
-            }
+        for (int i = 0; i < kTC; ++i) {
+          if (i >= nc) break;
+          const float cx = cand[i].x;
+          const int cid = cand[i].id;
+          float acc = 0.f;
+          unsigned int cnt = 0u;
+#pragma unroll
+          for (int m = 0; m < 32; ++m) {
+            const bool ahead = x[m] > cx || (x[m] == cx && member_id(bid, m) < cid);
+            acc += ahead ? e[m] : 0.f;
+            cnt += ahead ? 1u : 0u;
           }
+          msf[i] += acc;
+          ct[i] += cnt;
         }
       }
     }
+#pragma unroll
+    for (int i = 0; i < kTC; ++i) ms[i] = __float2ull_rn(msf[i] * 1099511627776.0f);
 #pragma unroll
     for (int i = 0; i < kTC; ++i) {
 #pragma unroll
@@ -2066,6 +2177,8 @@ template <typename T>
 cudaError_t prepare() {
   cudaError_t e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(RowSm)));
   if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kScanSmem));
+  if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decide_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmFull));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(retry_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDecSmFull));
@@ -2093,9 +2206,9 @@ int device_setup(int* sms) {
 }
 
 template <typename T>
-void launch_all(const Params& P, unsigned g1, int wpc, unsigned g2, size_t dec_smem, unsigned g3, unsigned g4,
+void launch_all(const Params& P, dim3 g1, unsigned g2, size_t dec_smem, unsigned g3, unsigned g4,
                 cudaStream_t stream) {
-  scan_kernel<T><<<g1, wpc * 32, 0, stream>>>(P);
+  scan_kernel<T><<<g1, kSumThreads, kScanSmem, stream>>>(P);
   decide_kernel<T><<<g2, kRowThreads, dec_smem, stream>>>(P);
   count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P, 0);
   retry_kernel<T><<<g4, kRowThreads, dec_smem, stream>>>(P);
@@ -2161,12 +2274,10 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   P.plist = reinterpret_cast<int*>(base + L.plist);
   P.rlist = reinterpret_cast<int*>(base + L.rlist);
   P.flist = reinterpret_cast<int*>(base + L.flist);
-  // scan: one warp per task; narrower CTAs when there are few tasks, so that
-  // they spread over the SMs
+  // scan: one warp per task, a 2-D grid of (task blocks, rows)
   const long long tasks = (long long)ka.batch * tb;
-  int wpc = kSumThreads / 32;
-  while (wpc > 1 && tasks < (long long)wpc * sms * 2) wpc >>= 1;
-  const unsigned g1 = unsigned((tasks + wpc - 1) / wpc);
+  const dim3 g1(unsigned((tb + kSumThreads / 32 - 1) / (kSumThreads / 32)),
+                unsigned(ka.batch < 65535 ? ka.batch : 65535));
   const unsigned g2 = unsigned(ka.batch);
   const bool pen = ka.history && ka.rep_penalties;
   const size_t dec_smem = pen ? kDecSmFull : kDecSmNoHash;
@@ -2174,9 +2285,9 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   const unsigned g3 = unsigned(cwarps < (long long)sms * 4 ? (cwarps < 1 ? 1 : cwarps) : (long long)sms * 4);
   const unsigned g4 = unsigned(ka.batch < (int64_t)sms * 2 ? ka.batch : (int64_t)sms * 2);
   switch (ka.dtype) {
-    case QE_DTYPE_F32: launch_all<float>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
-    case QE_DTYPE_BF16: launch_all<__nv_bfloat16>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
-    default: launch_all<__half>(P, g1, wpc, g2, dec_smem, g3, g4, stream); break;
+    case QE_DTYPE_F32: launch_all<float>(P, g1, g2, dec_smem, g3, g4, stream); break;
+    case QE_DTYPE_BF16: launch_all<__nv_bfloat16>(P, g1, g2, dec_smem, g3, g4, stream); break;
+    default: launch_all<__half>(P, g1, g2, dec_smem, g3, g4, stream); break;
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("stream sampler launch: ") + cudaGetErrorString(e));

@@ -104,7 +104,7 @@ inline int64_t stream_groups_per_row(int64_t V) {
   return n;
 }
 
-// Tiles per scan task: 2 for 16-bit rows and 1 for fp32 rows, doubled until
+// Tiles per scan task: 4 for 16-bit rows and 1 for fp32 rows, doubled until
 // no slice has more than kMaxTasksPerSlice tasks.
 inline int stream_tpw(int64_t V, int esize) {
   int64_t maxt = 0;
@@ -112,7 +112,7 @@ inline int stream_tpw(int64_t V, int esize) {
     const int64_t t = (slice_start(s + 1, V) - slice_start(s, V) + kTile - 1) / kTile;
     maxt = t > maxt ? t : maxt;
   }
-  int tpw = esize == 4 ? 1 : 2;
+  int tpw = esize == 4 ? 1 : 4;
   while ((maxt + tpw - 1) / tpw > kMaxTasksPerSlice) tpw *= 2;
   return tpw;
 }
