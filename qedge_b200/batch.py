@@ -3,15 +3,49 @@
 Extends the reference's ``Batch._fill_sampling`` (``src/data/batch.py:149-175``):
 the same structure-of-arrays on the device (``temperatures``, ``top_ps``,
 ``top_ks``, ``min_ps``), the same mapping of ``None``/<=0 top-k to the full
-vocabulary (``:154-157``), reusable pinned host staging and a signature
-cache that skips the upload when nothing changed (``:160-162``); plus the
-repetition-penalty arrays and a fixed-width token-history buffer the B200
-sampler reads.  The host flags ``all_greedy``/``use_top_p`` are computed as in
+vocabulary (``:154-157``) and a signature cache that skips the upload when
+nothing changed (``:160-162``); plus the repetition-penalty arrays and a
+fixed-width token-history buffer the B200 sampler reads.  The parameters
+live in one device block with a pinned host mirror, so a change is one
+host-to-device copy.  The host flags ``all_greedy``/``use_top_p`` are computed as in
 ``:169-174``.
 """
 from __future__ import annotations
 
 import torch
+
+
+class _Block:
+    """Device tensors carved from one contiguous device buffer, with a pinned
+    host mirror of the same layout: a whole block goes up in one copy.  An
+    event recorded after each copy is waited on before the host mirror is
+    written again, so a copy still in flight never sees new contents."""
+
+    def __init__(self, fields, device: torch.device):
+        self.device = device
+        nbytes = sum(n * torch.empty((), dtype=dt).element_size() for _, n, dt in fields)
+        self.dev = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=device)
+        pinned = device.type == "cuda"
+        self.host = torch.zeros(self.dev.numel(), dtype=torch.uint8, pin_memory=pinned)
+        self.views, self.host_views = {}, {}
+        off = 0
+        for name, n, dt in fields:
+            size = n * torch.empty((), dtype=dt).element_size()
+            self.views[name] = self.dev[off:off + size].view(dt)
+            self.host_views[name] = self.host[off:off + size].view(dt).numpy()
+            off += size
+        self.used = off
+        self._event = torch.cuda.Event() if pinned else None
+
+    def host_ready(self) -> None:
+        if self._event is not None:
+            self._event.synchronize()
+
+    def upload(self, nbytes: int | None = None) -> None:
+        n = self.used if nbytes is None else nbytes
+        self.dev[:n].copy_(self.host[:n], non_blocking=True)
+        if self._event is not None:
+            self._event.record()
 
 
 class SamplingBatch:
@@ -21,14 +55,19 @@ class SamplingBatch:
         self.vocab_size = vocab_size
         self.device = torch.device(device)
         self.history_width = history_width
-        d = self.device
-        self.temperatures = torch.zeros(max_bs, dtype=torch.float32, device=d)
-        self.top_ps = torch.zeros(max_bs, dtype=torch.float32, device=d)
-        self.top_ks = torch.zeros(max_bs, dtype=torch.int32, device=d)
-        self.min_ps = torch.zeros(max_bs, dtype=torch.float32, device=d)
-        self.rep_penalties = torch.ones(max_bs, dtype=torch.float32, device=d)
-        self.history = torch.zeros(max_bs, max(history_width, 1), dtype=torch.int32, device=d)
-        self.history_lens = torch.zeros(max_bs, dtype=torch.int32, device=d)
+        W = max(history_width, 1)
+        # per-row parameters in one block (one host-to-device copy per change)
+        self._params = _Block([("temperatures", max_bs, torch.float32), ("top_ps", max_bs, torch.float32),
+                               ("top_ks", max_bs, torch.int32), ("min_ps", max_bs, torch.float32),
+                               ("rep_penalties", max_bs, torch.float32)], self.device)
+        self._hist = _Block([("history_lens", max_bs, torch.int32), ("history", max_bs * W, torch.int32)],
+                            self.device)
+        v = self._params.views
+        self.temperatures, self.top_ps, self.top_ks = v["temperatures"], v["top_ps"], v["top_ks"]
+        self.min_ps, self.rep_penalties = v["min_ps"], v["rep_penalties"]
+        self.rep_penalties.fill_(1.0)
+        self.history_lens = self._hist.views["history_lens"]
+        self.history = self._hist.views["history"].view(max_bs, W)
         self.all_greedy = True
         self.any_greedy = False
         self.use_top_k = False
@@ -36,23 +75,8 @@ class SamplingBatch:
         self.use_min_p = False
         self.use_penalty = False
         self.max_top_k = 0
-        self._staging: dict[tuple[int, torch.dtype], torch.Tensor] = {}
         self._signature = None
         self._history_signature = None
-
-    def _pinned(self) -> bool:
-        return self.device.type == "cuda"
-
-    def _cp(self, dst: torch.Tensor, data: list, dtype: torch.dtype) -> None:
-        storage = dst.untyped_storage()
-        key = (storage.data_ptr(), dtype)
-        capacity = storage.nbytes() // torch.empty((), dtype=dtype).element_size()
-        cpu = self._staging.get(key)
-        if cpu is None or cpu.numel() < capacity:
-            cpu = torch.empty(capacity, dtype=dtype, pin_memory=self._pinned())
-            self._staging[key] = cpu
-        cpu.numpy()[:len(data)] = data
-        dst.copy_(cpu[:len(data)].view_as(dst), non_blocking=True)
 
     def fill(self, seqs) -> None:
         """Pack the sampling fields of ``seqs`` (objects with ``temperature``,
@@ -69,11 +93,15 @@ class SamplingBatch:
         rps = [float(getattr(s, "repetition_penalty", 1.0) or 1.0) for s in seqs]
         signature = tuple(zip(temps, top_ps, top_ks, min_ps, rps))
         if signature != self._signature:
-            self._cp(self.temperatures[:bs], temps, torch.float32)
-            self._cp(self.top_ps[:bs], top_ps, torch.float32)
-            self._cp(self.top_ks[:bs], top_ks, torch.int32)
-            self._cp(self.min_ps[:bs], min_ps, torch.float32)
-            self._cp(self.rep_penalties[:bs], rps, torch.float32)
+            blk = self._params
+            blk.host_ready()
+            hv = blk.host_views
+            hv["temperatures"][:bs] = temps
+            hv["top_ps"][:bs] = top_ps
+            hv["top_ks"][:bs] = top_ks
+            hv["min_ps"][:bs] = min_ps
+            hv["rep_penalties"][:bs] = rps
+            blk.upload()
             self.all_greedy = all(t <= 1e-5 for t in temps)
             self.any_greedy = any(t <= 1e-5 for t in temps)
             self.use_top_k = any(k < vocab for k in top_ks)
@@ -92,13 +120,15 @@ class SamplingBatch:
         sig = tuple((id(s), len(getattr(s, "token_ids", ()))) for s in seqs)
         if sig == self._history_signature:
             return
-        flat, lens = [], []
-        for s in seqs:
+        blk = self._hist
+        blk.host_ready()
+        lens = blk.host_views["history_lens"]
+        rows = blk.host_views["history"].reshape(self.max_bs, W)
+        for r, s in enumerate(seqs):
             ids = list(getattr(s, "token_ids", ()))[-W:]
-            lens.append(len(ids))
-            flat.extend(ids + [0] * (W - len(ids)))
-        self._cp(self.history[:len(seqs)].reshape(-1), flat, torch.int32)
-        self._cp(self.history_lens[:len(seqs)], lens, torch.int32)
+            lens[r] = len(ids)
+            rows[r, :len(ids)] = ids
+        blk.upload()
         self._history_signature = sig
 
     def sampler_kwargs(self, bs: int) -> dict:
