@@ -51,7 +51,7 @@ enum qe_row_status {
   QE_ROW_NONFINITE = 2,    /* probabilities not finite; greedy argmax returned */
   QE_ROW_GATHERED = 4,     /* diagnostic: finished from the gathered head of the row */
   QE_ROW_SLOW = 8,         /* diagnostic: finished by the exact (threshold + race) rounds */
-  QE_ROW_TIMEOUT = 16      /* a bounded wait on this row's data gave up; out_ids[row] = -1 */
+  QE_ROW_TIMEOUT = 16      /* reserved: no kernel of this library waits on another CTA or a flag */
 };
 
 typedef struct qe_sample_args {
@@ -77,8 +77,7 @@ typedef struct qe_sample_args {
   const uint64_t* step_ptr;    /* device step counter; overrides `step` when non-NULL */
   int64_t row_offset;          /* global index of row 0 (keys the Philox stream) */
   uint32_t flags;              /* enum qe_flags */
-  uint32_t wait_polls;         /* 0: default bound on every device-side wait (about a second);
-                                  n > 0: give up after n - 1 polls (tests of the timeout path) */
+  uint32_t wait_polls;         /* reserved, ignored: no kernel of this library spins on a wait */
   int64_t* out_ids;            /* [B] sampled token ids (int64, like torch.argmax) */
   float* out_probs;            /* [B, probs_ld] softmax probabilities or NULL */
   int64_t probs_ld;
@@ -106,9 +105,10 @@ int qe_sample(const qe_sample_args* args, void* stream);
 const char* qe_last_error(void);
 
 /* Device-side error bits of the last qe_sample call that used `workspace`
- * (1: a bounded wait gave up; its rows carry QE_ROW_TIMEOUT and id -1).
- * Waits for `stream`, then copies one word to the host.  This is the only
- * call of the library that synchronises the host. */
+ * on the default (streaming) path (4: a race found no candidate, which a row
+ * with finite probabilities cannot produce; its id is -1).  Waits for
+ * `stream`, then copies one word to the host.  This is the only call of the
+ * library that synchronises the host. */
 int qe_sample_errors(const void* workspace, void* stream, uint32_t* flags);
 
 /* Bytes of the scratch array built into the library for qe_sample_noalloc. */
@@ -122,7 +122,7 @@ int qe_sample_errors(const void* workspace, void* stream, uint32_t* flags);
  * every GPU that uses the library holds until the process exits.
  * `workspace` and `workspace_bytes` in args are ignored.  Calls whose
  * qe_sample_workspace_size(batch, vocab) exceeds the array are rejected with
- * QE_ERR_UNSUPPORTED (at V = 248,320 about 500 rows fit).  The first call on
+ * QE_ERR_UNSUPPORTED (at V = 248,320 up to 314 rows fit).  The first call on
  * a device looks up the array's device address; make that first call before
  * any stream capture.  All calls share the one array: calls that overlap on
  * the GPU (other streams, other host threads) race and must be serialised by

@@ -1970,14 +1970,16 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
   if (npend == 0u) return;
   const int* plist = P.plist + size_t(round) * size_t(P.a.batch);
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const long long items = (long long)npend * P.tasks_row;
+  const int tiles_row = int(P.G / 32);
+  const long long items = (long long)npend * tiles_row;   // one tile (32 groups, a lane each) per item
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
   const KernelArgs& a = P.a;
 #pragma unroll 1
   for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + wib; item < items; item += nw) {
-    const int row = plist[item / P.tasks_row];
-    const int t = int(item % P.tasks_row);
+    const int row = plist[item / tiles_row];
+    const int gt = int(item % tiles_row);   // global tile index: groups [gt*32, gt*32+32)
     RowState* rs = P.rstate + row;
+    const GroupSum sg = P.summ[size_t(row) * size_t(P.G) + size_t(gt) * 32 + lane];
     const int nc = rs->ncand;
     Cand cand[kTC];
     float xlo = INFINITY;
@@ -1996,59 +1998,47 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
       hl = hl < 0 ? 0 : (hl > int(a.history_ld) ? int(a.history_ld) : hl);
     }
     const bool pen = hl > 0 && !(rpen == 1.f);
-    const int32_t* hist = pen ? a.history + row * a.history_ld : nullptr;
     int s = 0;
-#pragma unroll 1
-    while (s + 1 < kNumSlices && P.tbase[s + 1] <= t) ++s;
-    const int tile0 = (t - P.tbase[s]) * P.tpw;
-    const int ntile = min(P.tpw, P.snt[s] - tile0);
+#pragma unroll
+    for (int step = 8; step > 0; step >>= 1)
+      if (s + step < kNumSlices && P.gbase[s + step] <= int64_t(gt) * 32) s += step;
+    const int tile = int((int64_t(gt) * 32 - P.gbase[s]) / 32);
     const int64_t sa = P.sstart[s];
     const int L = int(P.sstart[s + 1] - sa);
-    const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
-    const GroupSum* gs = P.summ + size_t(row) * size_t(P.G) + size_t(P.gbase[s] + int64_t(tile0) * 32);
+    if (pen) pen_bits_build(pen_bits[wib], a.history + row * a.history_ld, hl, sa, tile, 1, L);
     // per candidate: mass (fp32 per lane, then 2^-40 fixed point) and count
     // of the ids strictly ahead of it
     float msf[kTC] = {0.f, 0.f, 0.f, 0.f};
     unsigned long long ms[kTC], ct[kTC] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll 1
-    for (int tp = 0; tp < ntile; tp += 2) {
-      const int nt = min(2, ntile - tp);
-      if (pen) pen_bits_build(pen_bits[wib], hist, hl, sa, tile0 + tp, nt, L);
-      float gm2[2];
+    if (sg.gmax >= xlo) {
+      const unsigned char* src = static_cast<const unsigned char*>(a.logits) + (size_t(row) * size_t(a.ld) + size_t(sa)) * P.esize;
+      float x[32];
+      load_members<T>(P, src, tile, lane, L, x);
+      const uint32_t pb = pen ? pen_bits[wib][lane] : 0u;
+      if (pb) {
 #pragma unroll
-      for (int tt = 0; tt < 2; ++tt) gm2[tt] = tt < nt ? gs[(tp + tt) * 32 + lane].gmax : -INFINITY;
-#pragma unroll 1
-      for (int tt = 0; tt < nt; ++tt) {
-        const int tile = tile0 + tp + tt;
-        if (!(gm2[tt] >= xlo)) continue;
-        float x[32];
-        load_members<T>(P, src, tile, lane, L, x);
-        const uint32_t pb = pen ? pen_bits[wib][tt * 32 + lane] : 0u;
-        if (pb) {
+        for (int m = 0; m < 32; ++m)
+          if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
+      }
+      const int bid = int(sa) + tile * kTile + lane * 8;
+      float e[32];
 #pragma unroll
-          for (int m = 0; m < 32; ++m)
-            if ((pb >> m) & 1u) x[m] = pen_x(x[m], rpen);
+      for (int m = 0; m < 32; ++m) e[m] = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
+#pragma unroll
+      for (int i = 0; i < kTC; ++i) {
+        if (i >= nc) break;
+        const float cx = cand[i].x;
+        const int cid = cand[i].id;
+        float acc = 0.f;
+        unsigned int cnt = 0u;
+#pragma unroll
+        for (int m = 0; m < 32; ++m) {
+          const bool ahead = x[m] > cx || (x[m] == cx && member_id(bid, m) < cid);
+          acc += ahead ? e[m] : 0.f;
+          cnt += ahead ? 1u : 0u;
         }
-        const int bid = int(sa) + tile * kTile + lane * 8;
-        float e[32];
-#pragma unroll
-        for (int m = 0; m < 32; ++m) e[m] = qe_ex2_ftz(__fmaf_rn(x[m], c1, c0));
-#pragma unroll
-        for (int i = 0; i < kTC; ++i) {
-          if (i >= nc) break;
-          const float cx = cand[i].x;
-          const int cid = cand[i].id;
-          float acc = 0.f;
-          unsigned int cnt = 0u;
-#pragma unroll
-          for (int m = 0; m < 32; ++m) {
-            const bool ahead = x[m] > cx || (x[m] == cx && member_id(bid, m) < cid);
-            acc += ahead ? e[m] : 0.f;
-            cnt += ahead ? 1u : 0u;
-          }
-          msf[i] += acc;
-          ct[i] += cnt;
-        }
+        msf[i] = acc;
+        ct[i] = cnt;
       }
     }
 #pragma unroll
@@ -2069,7 +2059,7 @@ __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constan
       }
       __threadfence();
       const unsigned d = atomicAdd(&rs->done, 1u);
-      if (d == unsigned(P.tasks_row - 1)) {
+      if (d == unsigned(tiles_row - 1)) {
         __threadfence();
         // the row's counts are complete: first candidate inside the kept set
         const float tp_ = a.top_ps ? a.top_ps[row] : 1.f;
@@ -2281,7 +2271,7 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   const unsigned g2 = unsigned(ka.batch);
   const bool pen = ka.history && ka.rep_penalties;
   const size_t dec_smem = pen ? kDecSmFull : kDecSmNoHash;
-  const long long cwarps = (tasks + 7) / 8;
+  const long long cwarps = ((long long)ka.batch * (L.G / 32) + 7) / 8;
   const unsigned g3 = unsigned(cwarps < (long long)sms * 4 ? (cwarps < 1 ? 1 : cwarps) : (long long)sms * 4);
   const unsigned g4 = unsigned(ka.batch < (int64_t)sms * 2 ? ka.batch : (int64_t)sms * 2);
   switch (ka.dtype) {

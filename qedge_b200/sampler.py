@@ -74,9 +74,9 @@ class QESampler(nn.Module):
         return ws
 
     def device_errors(self, device=None) -> int:
-        """Error bits the last call on ``device`` left on the GPU (1: a bounded
-        wait gave up; those rows carry QE_ROW_TIMEOUT and id -1).  Waits for
-        the current stream."""
+        """Error bits the last call on ``device`` left on the GPU (4: a race
+        found no candidate; that row's id is -1).  Waits for the current
+        stream."""
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         key = dev.index if dev.index is not None else torch.cuda.current_device()
         ws = self._ws.get(key)
@@ -93,7 +93,7 @@ class QESampler(nn.Module):
         bits = self.device_errors(device)
         if bits:
             raise N.NativeError(f"sampler kernel reported device error bits {bits:#x} "
-                                f"(1: a bounded wait gave up; affected rows have id -1)")
+                                f"(4: a race found no candidate; affected rows have id -1)")
 
     @torch.no_grad()
     def forward(self, logits: torch.Tensor, temperatures: torch.Tensor,
