@@ -23,17 +23,19 @@ class _Block:
 
     def __init__(self, fields, device: torch.device):
         self.device = device
-        nbytes = sum(n * torch.empty((), dtype=dt).element_size() for _, n, dt in fields)
+        def size(n, dt):   # each field starts 16-byte aligned
+            return (n * torch.empty((), dtype=dt).element_size() + 15) // 16 * 16
+        nbytes = sum(size(n, dt) for _, n, dt in fields)
         self.dev = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=device)
         pinned = device.type == "cuda"
         self.host = torch.zeros(self.dev.numel(), dtype=torch.uint8, pin_memory=pinned)
         self.views, self.host_views = {}, {}
         off = 0
         for name, n, dt in fields:
-            size = n * torch.empty((), dtype=dt).element_size()
-            self.views[name] = self.dev[off:off + size].view(dt)
-            self.host_views[name] = self.host[off:off + size].view(dt).numpy()
-            off += size
+            nb = n * torch.empty((), dtype=dt).element_size()
+            self.views[name] = self.dev[off:off + nb].view(dt)
+            self.host_views[name] = self.host[off:off + nb].view(dt).numpy()
+            off += size(n, dt)
         self.used = off
         self._event = torch.cuda.Event() if pinned else None
 
@@ -59,12 +61,14 @@ class SamplingBatch:
         # per-row parameters in one block (one host-to-device copy per change)
         self._params = _Block([("temperatures", max_bs, torch.float32), ("top_ps", max_bs, torch.float32),
                                ("top_ks", max_bs, torch.int32), ("min_ps", max_bs, torch.float32),
-                               ("rep_penalties", max_bs, torch.float32)], self.device)
+                               ("rep_penalties", max_bs, torch.float32), ("seeds", max_bs, torch.int64)],
+                              self.device)
         self._hist = _Block([("history_lens", max_bs, torch.int32), ("history", max_bs * W, torch.int32)],
                             self.device)
         v = self._params.views
         self.temperatures, self.top_ps, self.top_ks = v["temperatures"], v["top_ps"], v["top_ks"]
-        self.min_ps, self.rep_penalties = v["min_ps"], v["rep_penalties"]
+        self.min_ps, self.rep_penalties, self.seeds = v["min_ps"], v["rep_penalties"], v["seeds"]
+        self.default_seed = 0
         self.rep_penalties.fill_(1.0)
         self.history_lens = self._hist.views["history_lens"]
         self.history = self._hist.views["history"].view(max_bs, W)
@@ -74,6 +78,7 @@ class SamplingBatch:
         self.use_top_p = False
         self.use_min_p = False
         self.use_penalty = False
+        self.use_seeds = False
         self.max_top_k = 0
         self._signature = None
         self._history_signature = None
@@ -91,7 +96,11 @@ class SamplingBatch:
         top_ks = [vocab if (s.top_k is None or s.top_k <= 0) else min(int(s.top_k), vocab) for s in seqs]
         min_ps = [0.0 if s.min_p is None else float(s.min_p) for s in seqs]
         rps = [float(getattr(s, "repetition_penalty", 1.0) or 1.0) for s in seqs]
-        signature = tuple(zip(temps, top_ps, top_ks, min_ps, rps))
+        seeds = [getattr(s, "seed", None) for s in seqs]
+        use_seeds = any(x is not None for x in seeds)
+        # rows without a seed of their own keep the sampler's seed
+        seeds = [self.default_seed if x is None else int(x) for x in seeds]
+        signature = tuple(zip(temps, top_ps, top_ks, min_ps, rps, seeds))
         if signature != self._signature:
             blk = self._params
             blk.host_ready()
@@ -101,6 +110,7 @@ class SamplingBatch:
             hv["top_ks"][:bs] = top_ks
             hv["min_ps"][:bs] = min_ps
             hv["rep_penalties"][:bs] = rps
+            hv["seeds"][:bs] = [x - (1 << 64) if x >= (1 << 63) else x for x in seeds]
             blk.upload()
             self.all_greedy = all(t <= 1e-5 for t in temps)
             self.any_greedy = any(t <= 1e-5 for t in temps)
@@ -108,6 +118,7 @@ class SamplingBatch:
             self.use_top_p = any(p < 1.0 for p in top_ps)
             self.use_min_p = any(m > 0.0 for m in min_ps)
             self.use_penalty = any(r != 1.0 for r in rps)
+            self.use_seeds = use_seeds
             self.max_top_k = max(top_ks) if self.use_top_k else 0
             self._signature = signature
         if self.use_penalty and self.history_width > 0:
@@ -134,6 +145,10 @@ class SamplingBatch:
     def sampler_kwargs(self, bs: int) -> dict:
         """Keyword arguments for ``QESampler.forward`` for rows ``0..bs-1``."""
         kw = {"top_ks": self.top_ks[:bs]}
+        if self.use_min_p:
+            kw["min_ps"] = self.min_ps[:bs]
+        if self.use_seeds:
+            kw["seeds"] = self.seeds[:bs]
         if self.use_penalty and self.history_width > 0:
             kw.update(rep_penalties=self.rep_penalties[:bs], history=self.history[:bs],
                       history_lens=self.history_lens[:bs])

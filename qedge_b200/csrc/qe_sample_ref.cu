@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "qe_common.cuh"
@@ -491,17 +492,24 @@ static int launch_typed(const KernelArgs& ka, cudaStream_t st) {
   return QE_OK;
 }
 
+// Kernel attributes are per-device state: set them once per device, under a
+// lock (host threads may drive several devices).
 int ref_path_prepare() {
-  static bool done = false;
-  if (done) return QE_OK;
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(QE_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return QE_OK;
   // the dynamic shared-memory bitmap of a whole row may exceed 48 KB
   const int max_bytes = 200 * 1024;
-  cudaError_t e = cudaSuccess;
   e = cudaFuncSetAttribute(threshold_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(threshold_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(threshold_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
   if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  done = true;
+  done[dev] = true;
   return QE_OK;
 }
 

@@ -84,7 +84,7 @@ struct Params {
   Ctl* ctl;
   GroupSum* summ;               // [B][G]
   TaskRec* trec;                // [B][tasks_row]
-  float* emin;                  // [B][G] noise minimum per group (caller-noise mode)
+  float* emin;                  // [B][G] per group: noise minimum (caller-noise mode) or bound key (Philox mode)
   RowState* rstate;             // [B]
   int* plist;                   // [2][B] rows queued for the count kernel (per round)
   int* rlist;                   // rows queued for the retry round
@@ -530,13 +530,16 @@ __device__ __forceinline__ void scan_task(const Params& P, int row, int t, uint4
         lo = emin_lower(wmin[tt]);
       }
       const float ug = __fmul_rn(r_.gmax, c1);
+      const float bkey = lo > 0.f ? ug - lg2_approx(lo) : INFINITY;
+      // Philox mode: the group's bound key itself, for the decide kernel's rescans
+      if (!nzrow) P.emin[size_t(row) * size_t(P.G) + size_t(g_first + gl)] = bkey;
       if (ug > lu) {
         lsum = __fmaf_rn(lsum, qe_ex2_ftz(__fsub_rn(lu, ug)), r_.aux);
         lu = ug;
       } else {
         lsum = __fmaf_rn(r_.aux, qe_ex2_ftz(__fsub_rn(ug, lu)), lsum);
       }
-      top.add(lo > 0.f ? ug - lg2_approx(lo) : INFINITY, int(g_first + gl));
+      top.add(bkey, int(g_first + gl));
     }
   }
   if (cp_ok) cp_async_wait<0>();   // no copy outlives the warp (tiles past the task's end were not issued)
@@ -1616,8 +1619,10 @@ __device__ __noinline__ bool race_round(const Params& P, DecSm& sm, const RowP& 
       const float gm = gms[k2];
       if (j >= ng || g == tr.bg0 || g == tr.bg1 || g == rp.s_gid) continue;
       if (!(gm > -INFINITY) || (rr.on && gm < rr.x)) continue;
-      const float lo = cnoise ? P.emin[size_t(row) * size_t(P.G) + size_t(g)] : emin_lower(group_min_word(rp.key, g));
-      const float bk = lo > 0.f ? __fmul_rn(gm, rp.c1) - lg2_approx(lo) : INFINITY;
+      // the group's bound key: stored by the scan kernel in Philox mode, from
+      // the group's noise minimum in caller-noise mode
+      const float ev = P.emin[size_t(row) * size_t(P.G) + size_t(g)];
+      const float bk = !cnoise ? ev : (ev > 0.f ? __fmul_rn(gm, rp.c1) - lg2_approx(ev) : INFINITY);
       if (bk >= lth) sm.gl[min(atomicAdd(&sm.ngl, 1), kGList - 1)] = int(g);
      }
     }

@@ -49,6 +49,7 @@ def install(runner, *, seed: int = 0, history_width: int = 2048) -> QESampler:
     runner.sampler = QESampler(seed=seed)
     runner.qe_batch = SamplingBatch(max_bs=max_bs, vocab_size=vocab, device=device,
                                     history_width=history_width)
+    runner.qe_batch.default_seed = int(seed) & ((1 << 64) - 1)
     runner.qe_step = 0
     runner._sample_gpu = types.MethodType(_sample_gpu, runner)
     cpu = getattr(runner, "sample_cpu", None)

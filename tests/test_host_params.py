@@ -78,3 +78,17 @@ def test_install_shim_wires_runner(monkeypatch):
     assert shape == (2, 50) and kw["use_top_p"] and kw["step"] == 0 and "history" in kw
     integration.uninstall(runner)
     assert runner.sampler == "orig" and runner._sample_gpu == "orig_fn"
+
+
+def test_batch_packs_per_request_seeds_and_min_p():
+    b = SamplingBatch(max_bs=3, vocab_size=100, device="cpu")
+    b.default_seed = 7
+    s0 = seq(1.0)
+    s1 = seq(0.8, 0.9)
+    s1.seed = 2**64 - 1
+    s1.min_p = 0.05
+    b.fill([s0, s1])
+    kw = b.sampler_kwargs(2)
+    assert "seeds" in kw and "min_ps" in kw
+    assert kw["seeds"].tolist() == [7, -1]              # uint64 bit patterns in int64
+    assert abs(kw["min_ps"][1].item() - 0.05) < 1e-7
