@@ -348,6 +348,13 @@ struct Top3 {
   }
 };
 
+// Programmatic dependent launch: the kernels after the scan are launched with
+// programmatic stream serialization, so they start during their
+// predecessor's tail; each waits here (a hardware dependency on the
+// predecessor grid's completion and memory flush, not a spin) before it
+// reads the predecessor's output.  Without such a launch it returns at once.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // cp.async (16 bytes, L2 only) and its group waits.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -1867,8 +1874,9 @@ __global__ void __launch_bounds__(kRowThreads) decide_kernel(const __grid_consta
   const int64_t V = P.a.vocab;
   const int ntask = P.tasks_row;
   const TaskRec* trg = P.trec + size_t(row) * size_t(ntask);
+  if (tid == 0) load_row_params(P, sm, row);   // inputs only: overlaps the scan's tail
+  wait_prior_grid();
   for (int i = tid; i < ntask; i += kRowThreads) sm.tr[i] = trg[i];
-  if (tid == 0) load_row_params(P, sm, row);
   __syncthreads();
   const RowP rp = sm.rp;
   const bool idx_mode = rp.kind == kKindGreedy || rp.kind == kKindArgmax;
@@ -1942,6 +1950,7 @@ template <typename T>
 __global__ void __launch_bounds__(kRowThreads) retry_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   DecSm& sm = *reinterpret_cast<DecSm*>(smem_raw);
+  wait_prior_grid();
   const unsigned nr = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_retry);
   const int tid = threadIdx.x;
   const int ntask = P.tasks_row;
@@ -1971,6 +1980,7 @@ __global__ void __launch_bounds__(kRowThreads) retry_kernel(const __grid_constan
 template <typename T>
 __global__ void __launch_bounds__(kSumThreads) count_kernel(const __grid_constant__ Params P, int round) {
   __shared__ uint32_t pen_bits[kSumThreads / 32][64];
+  wait_prior_grid();
   const unsigned npend = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_pend[round]);
   if (npend == 0u) return;
   const int* plist = P.plist + size_t(round) * size_t(P.a.batch);
@@ -2120,6 +2130,7 @@ template <typename T>
 __global__ void __launch_bounds__(kRowThreads) finish_kernel(const __grid_constant__ Params P) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   RowSm& sm = *reinterpret_cast<RowSm*>(smem_raw);
+  wait_prior_grid();
   const unsigned nfin = *reinterpret_cast<volatile unsigned*>(&P.ctl->n_fin);
   const int tid = threadIdx.x;
   const int64_t V = P.a.vocab;
@@ -2200,15 +2211,34 @@ int device_setup(int* sms) {
   return QE_OK;
 }
 
+// Launch with programmatic stream serialization (see wait_prior_grid).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename T>
-void launch_all(const Params& P, dim3 g1, unsigned g2, size_t dec_smem, unsigned g3, unsigned g4,
-                cudaStream_t stream) {
+cudaError_t launch_all(const Params& P, dim3 g1, unsigned g2, size_t dec_smem, unsigned g3, unsigned g4,
+                       cudaStream_t stream) {
   scan_kernel<T><<<g1, kSumThreads, kScanSmem, stream>>>(P);
-  decide_kernel<T><<<g2, kRowThreads, dec_smem, stream>>>(P);
-  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P, 0);
-  retry_kernel<T><<<g4, kRowThreads, dec_smem, stream>>>(P);
-  count_kernel<T><<<g3, kSumThreads, 0, stream>>>(P, 1);
-  finish_kernel<T><<<g4, kRowThreads, sizeof(RowSm), stream>>>(P);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = launch_dependent(decide_kernel<T>, dim3(g2), kRowThreads, dec_smem, stream, P);
+  if (e == cudaSuccess) e = launch_dependent(count_kernel<T>, dim3(g3), kSumThreads, 0, stream, P, 0);
+  if (e == cudaSuccess) e = launch_dependent(retry_kernel<T>, dim3(g4), kRowThreads, dec_smem, stream, P);
+  if (e == cudaSuccess) e = launch_dependent(count_kernel<T>, dim3(g3), kSumThreads, 0, stream, P, 1);
+  if (e == cudaSuccess) e = launch_dependent(finish_kernel<T>, dim3(g4), kRowThreads, sizeof(RowSm), stream, P);
+  return e;
 }
 
 }  // namespace st
@@ -2279,12 +2309,13 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   const long long cwarps = ((long long)ka.batch * (L.G / 32) + 7) / 8;
   const unsigned g3 = unsigned(cwarps < (long long)sms * 4 ? (cwarps < 1 ? 1 : cwarps) : (long long)sms * 4);
   const unsigned g4 = unsigned(ka.batch < (int64_t)sms * 2 ? ka.batch : (int64_t)sms * 2);
+  cudaError_t e;
   switch (ka.dtype) {
-    case QE_DTYPE_F32: launch_all<float>(P, g1, g2, dec_smem, g3, g4, stream); break;
-    case QE_DTYPE_BF16: launch_all<__nv_bfloat16>(P, g1, g2, dec_smem, g3, g4, stream); break;
-    default: launch_all<__half>(P, g1, g2, dec_smem, g3, g4, stream); break;
+    case QE_DTYPE_F32: e = launch_all<float>(P, g1, g2, dec_smem, g3, g4, stream); break;
+    case QE_DTYPE_BF16: e = launch_all<__nv_bfloat16>(P, g1, g2, dec_smem, g3, g4, stream); break;
+    default: e = launch_all<__half>(P, g1, g2, dec_smem, g3, g4, stream); break;
   }
-  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(QE_ERR_CUDA, std::string("stream sampler launch: ") + cudaGetErrorString(e));
   return QE_OK;
 }
