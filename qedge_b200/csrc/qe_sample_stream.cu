@@ -1581,7 +1581,7 @@ struct Restr {
 // complete above theta.  Returns false when a capacity ran out (the row
 // then takes the exact path).
 template <typename T>
-__device__ __noinline__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
+__device__ __forceinline__ bool race_round(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float c0, float Sf,
                            float theta, const Restr& rr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ntask = P.tasks_row;
@@ -1742,7 +1742,7 @@ __device__ __forceinline__ void push_fin(const Params& P, int row, unsigned kind
 // to the ids ahead of it.  Undecided candidates go to the count kernel of
 // `round`; rows still open after the rounds go to the finish kernel.
 template <typename T>
-__device__ __noinline__ void sample_rounds(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float Sf, double S,
+__device__ __forceinline__ void sample_rounds(const Params& P, DecSm& sm, const RowP& rp, int row, float u, float Sf, double S,
                               float thr_m, Restr rr, int round) {
   const int tid = threadIdx.x;
   const int ntask = P.tasks_row;
@@ -1754,11 +1754,14 @@ __device__ __noinline__ void sample_rounds(const Params& P, DecSm& sm, const Row
   const int G = int(P.G);
 #pragma unroll 1
   for (int it = 0; it < 3; ++it) {
+    // one call site of the race (complete above 1/4, else above 1/16)
     float theta = 0.25f;
-    bool ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta, rr);
-    if (ok && !(sm.ntop > 0 && sm.top[0].r >= theta)) {
-      theta = 0.0625f;
+    bool ok = false;
+#pragma unroll 1
+    for (int rnd = 0; rnd < 2; ++rnd) {
+      theta = rnd == 0 ? 0.25f : 0.0625f;
       ok = race_round<T>(P, sm, rp, row, u, c0, Sf, theta, rr);
+      if (!ok || (sm.ntop > 0 && sm.top[0].r >= theta)) break;
     }
     if (!ok || !(sm.ntop > 0 && sm.top[0].r >= theta)) break;
     if (!rp.filtered) {
