@@ -1331,7 +1331,7 @@ __device__ uint32_t kth_group_key(const Params& P, RowSm& sm, int row, int k) {
 // (reference rule), and the kept ones raced with exact noise.  Returns false
 // when a capacity ran out (the caller takes the exact path).
 template <typename T>
-__device__ __noinline__ bool small_k(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float thr_m) {
+__device__ __forceinline__ bool small_k(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, float thr_m) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = int(rp.k);
   const uint32_t tk = kth_group_key(P, sm, row, k);
