@@ -658,6 +658,8 @@ struct alignas(16) RowSm {
       unsigned int cnt[256];
       unsigned long long mass[256];
       unsigned int nm;
+      unsigned int cntw[kRowWarps][256];          // per-warp copies: less atomic contention
+      unsigned long long massw[kRowWarps][256];
     } h;
     unsigned long long keys[kSelCap];
     struct {
@@ -1057,7 +1059,7 @@ __device__ __forceinline__ unsigned long long efix(float x, float c1, float c0) 
 template <typename T>
 __device__ __noinline__ void exact_path(const Params& P, RowSm& sm, const RowP& rp, int row, float c0, float Sf, double S,
                            float thr_m, float xf) {
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int final_level = rp.pen ? 3 : P.dtype_level;
   const float c1 = rp.c1;
   if (thr_m > 0.f) xf = -INFINITY;   // the min-p count needs every id
@@ -1072,9 +1074,9 @@ __device__ __noinline__ void exact_path(const Params& P, RowSm& sm, const RowP& 
   if (tid == 0) sm.bcast = 0;
 #pragma unroll 1
   for (int L = 0; L < 4; ++L) {
-    for (int i = tid; i < 256; i += kRowThreads) {
-      sm.u.h.cnt[i] = 0u;
-      sm.u.h.mass[i] = 0ull;
+    for (int i = tid; i < kRowWarps * 256; i += kRowThreads) {
+      (&sm.u.h.cntw[0][0])[i] = 0u;
+      (&sm.u.h.massw[0][0])[i] = 0ull;
     }
     if (tid == 0) sm.u.h.nm = 0u;
     __syncthreads();
@@ -1093,14 +1095,26 @@ __device__ __noinline__ void exact_path(const Params& P, RowSm& sm, const RowP& 
         const uint32_t k = ordered_key(v);
         if (L > 0 && (k >> (32 - 8 * L)) != pre) continue;
         const int bin = int((k >> shift) & 255u);
-        atomicAdd(&sm.u.h.cnt[bin], 1u);
-        atomicAdd(&sm.u.h.mass[bin], efix(v, c1, c0));
+        atomicAdd(&sm.u.h.cntw[warp][bin], 1u);
+        atomicAdd(&sm.u.h.massw[warp][bin], efix(v, c1, c0));
         if (L == 0 && thr_m > 0.f && __fdiv_rn(qe_ex2_ftz(__fmaf_rn(v, c1, c0)), Sf) >= thr_m) ++nm;
       }
     };
     lane_visit<T, false>(P, sm, rp, row, want, vis);
     nm = __reduce_add_sync(0xFFFFFFFFu, nm);
     if (lane == 0 && nm) atomicAdd(&sm.u.h.nm, nm);
+    __syncthreads();
+    for (int b = tid; b < 256; b += kRowThreads) {
+      unsigned int c = 0u;
+      unsigned long long ms = 0ull;
+#pragma unroll
+      for (int w = 0; w < kRowWarps; ++w) {
+        c += sm.u.h.cntw[w][b];
+        ms += sm.u.h.massw[w][b];
+      }
+      sm.u.h.cnt[b] = c;
+      sm.u.h.mass[b] = ms;
+    }
     __syncthreads();
     if (tid == 0) {
       int next = 0;
@@ -2303,7 +2317,6 @@ int launch_stream(const KernelArgs& ka, cudaStream_t stream) {
   P.rlist = reinterpret_cast<int*>(base + L.rlist);
   P.flist = reinterpret_cast<int*>(base + L.flist);
   // scan: one warp per task, a 2-D grid of (task blocks, rows)
-  const long long tasks = (long long)ka.batch * tb;
   const dim3 g1(unsigned((tb + kSumThreads / 32 - 1) / (kSumThreads / 32)),
                 unsigned(ka.batch < 65535 ? ka.batch : 65535));
   const unsigned g2 = unsigned(ka.batch);
