@@ -124,7 +124,8 @@ int qe_sample_errors(const void* workspace, void* stream, uint32_t* flags);
  * qe_sample_workspace_size(batch, vocab) exceeds the array are rejected with
  * QE_ERR_UNSUPPORTED (at V = 248,320 up to 314 rows fit).  The first call on
  * a device looks up the array's device address; make that first call before
- * any stream capture.  All calls share the one array: calls that overlap on
+ * any stream capture.  The address is kept for the life of the process: it
+ * does not survive cudaDeviceReset or a new primary context on that device.  All calls share the one array: calls that overlap on
  * the GPU (other streams, other host threads) race and must be serialised by
  * the caller.  No part of the array needs to start at zero: every kernel
  * writes the scratch it reads first.  Allocates nothing. */

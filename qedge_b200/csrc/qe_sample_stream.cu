@@ -1,5 +1,5 @@
 // qe_sample_stream.cu — the default sampler path: the logits read from HBM
-// once, four launches.
+// once, six launches on the caller's stream.
 //
 // Replaces BatchSampler.forward (src/compute/sampler.py:25-41) and the
 // extensions of this library (top-k, min-p, repetition penalty, Philox
@@ -8,25 +8,31 @@
 // prefix of the order (x desc, id asc) allowed by top-k, top-p and min-p,
 // token = argmax over the kept set of rho = RN(RN(e/S)/E).
 //
-// 1. scan_kernel streams the logits: one warp per task of `tpw` tiles (4 KB
-//    of bf16 logits per pair of tiles), each lane one 32-id group at a time
-//    held in registers (16-byte loads), reduced to a GroupSum (max,
-//    group-relative exponential sum); per task a TaskRec: max, sum in the
-//    task's scale, and the two largest group noise bounds with a ceiling for
-//    the rest (one Philox call per four groups).  No barriers.
+// 1. scan_kernel streams the logits: one warp per task of `tpw` tiles (8 KB
+//    of bf16 logits), copied into shared memory with cp.async before any
+//    arithmetic; each lane reduces one 32-id group at a time to a GroupSum
+//    (max, group-relative exponential sum, packed bf16x2 / f32x2 math) and
+//    its noise bound key; per task a TaskRec: max, sum in the task's scale,
+//    the two largest group bound keys with a ceiling for the rest (one Philox
+//    call per four groups).  No barriers.
 // 2. decide_kernel, one CTA per row, from the task records (still in L2):
 //      * row max, softmax normaliser S, greedy / top-1 / non-finite rows;
 //      * the exponential race over the groups whose bound reaches 1/4 (the
 //        best ratio of a race is below that with probability e^-4), then
-//        1/64: one group per thread, re-read and raced exactly;
+//        1/16: one group per thread, re-read and raced exactly;
 //      * the kept-set test of the 4 best candidates from the task records,
-//        then from the group records of the tasks that can hold ids ahead.
+//        then from the group records; a candidate outside the kept set
+//        restricts the next race to the ids ahead of it.
 // 3. count_kernel counts exactly, over all SMs, the ids ahead of the
 //    candidates of the rows the records could not settle; the warp that
-//    completes a row decides it (no waiting on other CTAs).
-// 4. finish_kernel (persistent CTAs) takes the rest: top-k rows with
-//    k <= 64 (the k largest, sorted) and the exact fallback (radix rounds
-//    over the keys, the tie rank, the race over the kept set).
+//    completes a row decides it (an atomic counter, no waiting).
+// 4. retry_kernel races again, restricted, the rows whose counted candidates
+//    were all outside the kept set; 5. count_kernel counts those.
+// 6. finish_kernel (persistent CTAs) takes the rest: top-k rows with
+//    k <= 64 (the k largest, sorted), rows whose kept-set size is asked for,
+//    and the exact fallback (radix rounds over the keys, the tie rank, the
+//    race over the kept set).
+// Launches 2-6 use programmatic stream serialization (wait_prior_grid).
 // No kernel waits for another CTA or on any flag.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>

@@ -1,6 +1,7 @@
 // qe_stream.cuh — data layout of the streaming sampler (qe_sample_stream.cu).
 //
-// The sampler runs as four launches.  The scan kernel streams every row of
+// The sampler runs as six launches (scan, decide, count, retry, count,
+// finish).  The scan kernel streams every row of
 // logits from HBM once, one warp per task of `tpw` tiles of 1024 ids inside a
 // canonical slice.  It reduces each 32-id group (the canonical layout of
 // qe_common.cuh) to a GroupSum and each task to a TaskRec.  The decide kernel
@@ -8,9 +9,10 @@
 // normaliser, the exponential race over the few groups whose noise bound can
 // win, and the kept-set test of the race candidates.  Rows whose test the
 // records cannot settle are counted exactly by the count kernel (all SMs over
-// the (row, task) pairs of those rows); rows that need the full kept set (all
-// candidates outside it, small top-k, out_kept asked for) are finished by the
-// finish kernel.
+// the (row, tile) pairs of those rows); rows whose counted candidates all lie
+// outside the kept set race again in the retry kernel; rows that need the
+// full kept set (small top-k, out_kept asked for, the rare rest) are finished
+// by the finish kernel.
 #pragma once
 #include <cstddef>
 #include <cstdint>
