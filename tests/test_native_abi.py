@@ -83,3 +83,16 @@ def test_workspace_size_monotone():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(N.NativeError):
         N.load(tmp_path / "nope.so")
+
+
+def test_workspace_sizes_and_noalloc_capacity():
+    """The workspace grows linearly with the batch, and the built-in scratch
+    of qe_sample_noalloc holds 314 rows at V = 248,320 (the documented limit)."""
+    from qedge_b200 import _native as N
+    lib = N.load()
+    V = 248_320
+    w1, w2 = lib.qe_sample_workspace_size(1, V), lib.qe_sample_workspace_size(2, V)
+    assert 0 < w1 < w2 and w2 - w1 < 120_000
+    assert lib.qe_sample_workspace_size(314, V) <= N.QE_NOALLOC_SCRATCH_BYTES
+    assert lib.qe_sample_workspace_size(315, V) > N.QE_NOALLOC_SCRATCH_BYTES
+    assert lib.qe_sample_workspace_size(0, V) == 0
